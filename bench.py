@@ -1,0 +1,512 @@
+#!/usr/bin/env python
+"""Benchmark of the CWLB-SpMM hot path on B200: FP32 CSR mean aggregation.
+
+One step = one mean-aggregation pass out[i,:] = (1/deg_i) sum_j A_ij X[j,:]
+over the whole (sharded) graph of the configuration, with the reordered CSR,
+X and the task list resident in HBM.  The metric is BASELINE.json's:
+GFLOP/s (2 * nnz * K per step) with HBM GB/s against the measured roofline.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--S S]
+  python bench.py --impl reference ...   (the CPU implementation of the path)
+
+Multi-GPU (torchrun, one rank per GPU): every rank builds the same graph,
+takes a contiguous, cost-balanced block of ORIGINAL rows (X replicated), sorts
+and partitions it on its GPU, and aggregates it; no collective on the data
+path.  Total work is fixed as N grows ("strong" scaling).
+
+Outside the timed region: graph synthesis (torch, seeded), degree sort,
+partition (both on the GPU), the S choice (the reference's --candidates
+procedure), task validation.  Inside: the aggregation launches only
+(device-resident value); `e2e` times the host-buffer C-ABI call
+(cwlb_spmm_kernel) with the H2D copy of every input and the D2H copy of the
+output inside each step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "cwlb-spmm_b200"), os.path.join(ROOT, "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import graphs  # noqa: E402
+
+# Cost weights used to partition (ns x 10 per operation, spmm_costs.txt order).
+COSTS_FILE = os.path.join(ROOT, "cwlb-spmm_b200", "resources", "spmm_costs.txt")
+PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, default=2, help="BASELINE.json config (1-5)")
+    ap.add_argument("--S", type=int, default=0, help="segment size; 0 = candidate search")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="target CPU time of the CPU-baseline sample")
+    return ap.parse_args()
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def read_costs():
+    import cwlb_spmm as cs
+    c = cs.read_costs_one_per_line(COSTS_FILE)
+    if c is None:
+        raise RuntimeError(f"cannot read {COSTS_FILE}")
+    return c
+
+
+def hbm_peak():
+    try:
+        with open(PEAKS_FILE) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.gpus = ",".join(str(i) for i in gpu_indices)
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpus, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def allreduce_max(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------
+# workload
+
+def shard_bounds(rowoff_t, costs, world, rank):
+    """Contiguous block of original rows with ~1/world of the total cost
+    (full_w = (Cc + Cl) deg + Cs per row)."""
+    import torch
+    if world == 1:
+        return 0, rowoff_t.numel() - 1
+    deg = (rowoff_t[1:] - rowoff_t[:-1]).to(torch.float64)
+    w = deg * (costs.C_compute_ns + costs.C_load_ns) + costs.C_store_ns
+    cum = torch.cumsum(w, 0)
+    total = float(cum[-1])
+    n = deg.numel()
+
+    def cut(k):
+        if k == 0:
+            return 0
+        if k == world:
+            return n
+        return int(torch.searchsorted(cum, total * k / world).item()) + 1
+
+    return min(cut(rank), n), min(cut(rank + 1), n)
+
+
+def build_workload(cfg_id, device, world, rank, costs):
+    import torch
+    rowoff, col, val, X = graphs.build_config_torch(cfg_id, device)
+    a, b = shard_bounds(rowoff, costs, world, rank)
+    e0, e1 = int(rowoff[a]), int(rowoff[b])
+    ro = (rowoff[a:b + 1] - e0).contiguous()
+    sub_col = col[e0:e1].contiguous()
+    sub_val = val[e0:e1].contiguous()
+    return dict(rowoff=ro, col=sub_col, val=sub_val, X=X, n=b - a, nnz=e1 - e0, row0=a,
+                nnz_total=int(rowoff[-1]), n_total=rowoff.numel() - 1, K=X.shape[1],
+                distinct_cols=int(torch.unique(sub_col).numel()) if e1 > e0 else 0)
+
+
+def device_prepare(ctx, wl):
+    import torch
+    dev = wl["X"].device
+    n, nnz = wl["n"], wl["nnz"]
+    org = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+    sro = torch.empty(n + 1, dtype=torch.int32, device=dev)
+    scol = torch.empty(max(nnz, 1), dtype=torch.int32, device=dev)
+    sval = torch.empty(max(nnz, 1), dtype=torch.float32, device=dev)
+    ctx.sort_by_degree_device(n, nnz, wl["rowoff"].data_ptr(), wl["col"].data_ptr(),
+                              wl["val"].data_ptr(), org.data_ptr(), sro.data_ptr(),
+                              scol.data_ptr(), sval.data_ptr())
+    torch.cuda.synchronize()
+    wl.update(org=org, sro=sro, scol=scol, sval=sval)
+
+
+def partition(ctx, wl, costs, S):
+    import torch
+    import cwlb_spmm as cs
+    cap = cs.capacity_from_s(S, costs)
+    t_ptr, n_tasks = ctx.partition_device(wl["n"], wl["sro"].data_ptr(), costs, cap)
+    tasks = torch.empty((max(n_tasks, 1), 4), dtype=torch.int32, device=wl["X"].device)
+    if n_tasks:
+        # own copy: the context's task buffer is reused by the next partition
+        src = torch.as_tensor(_DevPtr(t_ptr, n_tasks * 4), device=wl["X"].device)
+        tasks[:n_tasks].copy_(src.view(n_tasks, 4))
+    torch.cuda.synchronize()
+    chk = ctx.tasks_check(wl["n"], wl["nnz"], wl["sro"].data_ptr(), tasks.data_ptr(), n_tasks)
+    return tasks, n_tasks, cap, chk
+
+
+class _DevPtr:
+    """Minimal __cuda_array_interface__ wrapper over an int32 device buffer."""
+
+    def __init__(self, ptr, count):
+        self.__cuda_array_interface__ = {"shape": (count,), "typestr": "<i4",
+                                         "data": (ptr, False), "version": 3}
+
+
+def run_step(ctx, wl, tasks, n_tasks, out, flags):
+    ctx.spmm_mean_device(wl["n"], wl["nnz"], wl["sro"].data_ptr(), wl["scol"].data_ptr(),
+                         wl["sval"].data_ptr(), wl["org"].data_ptr(), wl["X"].data_ptr(),
+                         wl["X"].shape[0], wl["K"], tasks.data_ptr(), n_tasks, out.data_ptr(),
+                         flags)
+
+
+def time_steps(ctx, wl, tasks, n_tasks, out, flags, steps):
+    import torch
+    s = torch.cuda.current_stream()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        run_step(ctx, wl, tasks, n_tasks, out, flags)
+    e1.record(s)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / 1e3  # seconds
+
+
+def compulsory_bytes(n, nnz, n_tasks, K, x_rows):
+    """Algorithmic bytes of one aggregation pass: offsets, column ids and
+    values, Origin_local, the task list, every referenced X row once, every
+    output row once."""
+    return 4 * (n + 1) + 8 * nnz + 4 * n + 16 * n_tasks + 4 * x_rows * K + 4 * n * K
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle (restatement of the reference's kernel semantics)
+
+def cpu_baseline(wl, tasks_np, target_seconds):
+    from oracle import Oracle
+    oracle = Oracle()
+    srow = wl["sro"].cpu().numpy()
+    scol = wl["scol"][:wl["nnz"]].cpu().numpy()
+    sval = wl["sval"][:wl["nnz"]].cpu().numpy()
+    org = wl["org"][:wl["n"]].cpu().numpy()
+    X = wl["X"].cpu().numpy()
+    K = wl["K"]
+    threads = os.cpu_count() or 1
+    # nnz covered by a contiguous slice of tasks starting in the middle of the list
+    task_nnz = _task_nnz(srow, tasks_np)
+
+    def run(t0, t1):
+        sub = np.ascontiguousarray(tasks_np[t0:t1])
+        s = time.perf_counter()
+        oracle.spmm_mean(srow, scol, sval, org, X, sub, n_threads=threads)
+        return time.perf_counter() - s, int(task_nnz[t0:t1].sum())
+
+    n_t = len(tasks_np)
+    start = n_t // 3
+    probe = max(1, min(n_t - start, n_t // 200 + 1))
+    dt, nz = run(start, start + probe)
+    rate = max(nz, 1) / max(dt, 1e-6)
+    want_nnz = rate * target_seconds
+    csum = np.cumsum(task_nnz[start:])
+    t1 = start + int(np.searchsorted(csum, want_nnz)) + 1
+    t1 = min(max(t1, start + 1), n_t)
+    dt, nz = run(start, t1)
+    return {"value": 2.0 * nz * K / dt / 1e9, "unit": "GFLOP/s", "cores": threads,
+            "kind": "port",
+            "sample": f"oracle spmm_mean over tasks [{start}, {t1}) = {nz} nnz of {wl['nnz']} "
+                      f"(K={K}), {dt:.1f} s, {threads} OpenMP threads"}
+
+
+def _task_nnz(srow, tasks):
+    rs, re_, fo, ln = tasks[:, 0], tasks[:, 1], tasks[:, 2], tasks[:, 3]
+    total = srow[re_].astype(np.int64) - srow[rs].astype(np.int64)
+    total -= fo
+    last_deg = srow[re_] - srow[re_ - 1]
+    total -= np.where(ln > 0, last_deg - ln, 0)
+    return total
+
+
+# ---------------------------------------------------------------------------
+
+def run_ours(args):
+    import torch
+    import cwlb_spmm as cs
+    world, rank, local = dist_setup(args)
+    assert world == args.gpus or world == 1, "launch with torchrun for --gpus > 1"
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    costs = read_costs()
+    cfg = graphs.CONFIGS[args.config]
+    wl = build_workload(args.config, device, world, rank, costs)
+    ctx = cs.Context(local)
+    ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+    device_prepare(ctx, wl)
+    K = wl["K"]
+    out = torch.empty((max(wl["n"], 1), K), dtype=torch.float32, device=device)
+
+    # S: the reference's --candidates procedure (main.cpp:534-577): three
+    # wave-based S values from the nnz-keyed w table, keep the fastest.
+    cus = ctx.device_info()["max_compute_units"]
+    if args.S > 0:
+        candidates = [args.S]
+    elif cfg["S"]:
+        candidates = [cfg["S"]]
+    else:
+        ws = cs.recommended_candidate_w(wl["nnz_total"])
+        candidates = [cs.wave_based_s(wl["nnz_total"], cus, w) for w in ws]
+    best = None
+    for S in candidates:
+        tasks, n_tasks, cap, chk = partition(ctx, wl, costs, S)
+        flags = cs.ROWS_COVERED if (chk["uncovered_rows"] == 0 and chk["bad_tasks"] == 0 and
+                                    chk["nnz_coverage_errors"] == 0) else 0
+        for _ in range(3):
+            run_step(ctx, wl, tasks, n_tasks, out, flags)
+        t = allreduce_max(time_steps(ctx, wl, tasks, n_tasks, out, flags, 10) / 10, world)
+        log(f"[rank {rank}] candidate S={S}: {n_tasks} tasks, {t * 1e6:.1f} us/step")
+        if best is None or t < best[0]:
+            best = (t, S)
+    S = best[1]
+    tasks, n_tasks, cap, chk = partition(ctx, wl, costs, S)
+    covered = chk["uncovered_rows"] == 0 and chk["bad_tasks"] == 0 and chk["nnz_coverage_errors"] == 0
+    flags = cs.ROWS_COVERED if covered else 0
+
+    for _ in range(args.warmup):
+        run_step(ctx, wl, tasks, n_tasks, out, flags)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(list(range(world)) if world > 1 else [local]) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    t_local = time_steps(ctx, wl, tasks, n_tasks, out, flags, args.steps)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    assert ctx.take_device_errors() == 0
+    t_max = allreduce_max(t_local, world)
+
+    flops_total = 2.0 * wl["nnz_total"] * K
+    value = flops_total / (t_max / args.steps) / 1e9
+    per_launch = t_local / args.steps
+    bytes_local = compulsory_bytes(wl["n"], wl["nnz"], n_tasks, K, wl["distinct_cols"])
+    peak, peak_kind = hbm_peak()
+    achieved = bytes_local / per_launch / 1e9
+
+    # e2e: host buffers through the reference-facing call (spmmKernel)
+    sro = wl["sro"].cpu().pin_memory()
+    scol = wl["scol"][:wl["nnz"]].cpu().pin_memory()
+    sval = wl["sval"][:wl["nnz"]].cpu().pin_memory()
+    org = wl["org"][:wl["n"]].cpu().pin_memory()
+    Xh = wl["X"].cpu().pin_memory()
+    th = tasks[:n_tasks].cpu().pin_memory()
+    outh = torch.empty((wl["n"], K), dtype=torch.float32).pin_memory()
+    order = cs.CSR_Order(sro.numpy(), scol.numpy(), sval.numpy(), org.numpy())
+    call = ctx.spmmKernel if K <= 1024 else ctx.spmmKernelLargeKFallback
+    call(order, Xh.numpy(), K, K, th.numpy(), out=outh.numpy())  # warm
+    e2e_steps = max(1, min(args.e2e_steps, args.steps))
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        call(order, Xh.numpy(), K, K, th.numpy(), out=outh.numpy())
+    t_e2e = allreduce_max(time.perf_counter() - t0, world)
+    h2d = (sro.numel() + scol.numel() + sval.numel() + org.numel() + Xh.numel() +
+           th.numel()) * 4
+    d2h = outh.numel() * 4
+
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu = cpu_baseline(wl, tasks[:n_tasks].cpu().numpy(), args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": "SpMM GFLOP/s (2*nnz*K) and HBM GB/s vs roofline",
+            "value": round(value, 2), "unit": "GFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_max / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded generator, unit edge values)",
+            "config": {"workload": f"config {args.config}: {cfg['name']}",
+                       "rows": wl["n_total"], "nnz": wl["nnz_total"], "K": K, "S": S,
+                       "n_tasks_rank0": n_tasks, "costs": os.path.relpath(COSTS_FILE, ROOT),
+                       "parallelism": f"row shards x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (CSR + X > 126 MB), no flush",
+                       "hbm_gbs_rank0": round(achieved, 1)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": peak_kind, "traffic": None,
+                         "algorithmic_bytes_per_launch": bytes_local,
+                         "launch_us": round(per_launch * 1e6, 2)},
+            "e2e": {"value": round(flops_total / (t_e2e / e2e_steps) / 1e9, 2), "unit": "GFLOP/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": round(t_e2e / e2e_steps * 1e3, 3)},
+            "gpu_launches": (2 if flags else 1) * args.steps,
+            "clocks": clocks,
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    """The CPU implementation of the path (the oracle's restatement of the
+    reference kernel; the reference ships no CPU SpMM and its SYCL kernel
+    cannot be built here), timed on the host cores."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    from oracle import Oracle
+    oracle = Oracle()
+    cfg = graphs.CONFIGS[args.config]
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    rowoff, col, val, X = graphs.build_config_torch(args.config, dev)  # input synthesis only
+    rowoff, col, val, X = (t.cpu().numpy() for t in (rowoff, col, val, X))
+    costs = np.loadtxt(COSTS_FILE)[:4]
+    origin, srow, scol, sval = oracle.sort_by_degree(rowoff, col, val)
+    nnz = len(col)
+    K = X.shape[1]
+    if args.S > 0:
+        S = args.S
+    elif cfg["S"]:
+        S = cfg["S"]
+    else:
+        S = oracle.wave_based_s(nnz, 148, oracle.recommended_w(nnz)[0])
+    tasks = oracle.partition(srow, costs, oracle.capacity_from_s(S, costs))
+    wl = dict(sro=torch.from_numpy(srow), scol=torch.from_numpy(scol),
+              sval=torch.from_numpy(sval), org=torch.from_numpy(origin), X=torch.from_numpy(X),
+              K=K, nnz=nnz, n=len(origin))
+    per_step = max(1.0, 150.0 / max(args.steps + args.warmup, 1))
+    for _ in range(args.warmup):
+        cpu_baseline(wl, tasks, min(per_step, 2.0))
+    vals, samples = [], []
+    for _ in range(args.steps):
+        r = cpu_baseline(wl, tasks, per_step)
+        vals.append(r["value"])
+        samples.append(r)
+    v = statistics.mean(vals)
+    line = {"impl": "reference", "metric": "SpMM GFLOP/s (2*nnz*K) and HBM GB/s vs roofline",
+            "value": round(v, 3), "unit": "GFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator)",
+            "config": {"workload": f"config {args.config}: {cfg['name']}", "rows": len(origin),
+                       "nnz": nnz, "K": K, "S": S},
+            "cpu_baseline": {"value": round(v, 3), "unit": "GFLOP/s",
+                             "cores": samples[-1]["cores"], "kind": "port",
+                             "sample": samples[-1]["sample"] + " (per step)"},
+            "e2e": {"value": round(v, 3), "unit": "GFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,488 @@
+// C ABI of libcwlb_spmm: contexts, error reporting and the host-buffer entry
+// points that mirror the reference's synchronous functions.  Every exported
+// function converts internal failures into a cwlb_status and a thread-local
+// message; no C++ exception crosses the boundary.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <filesystem>
+#include <fstream>
+#include <iomanip>
+#include <limits>
+#include <string>
+
+#include "common.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+template <typename F>
+int guarded(F&& f) {
+    try {
+        f();
+        return CWLB_OK;
+    } catch (const cwlb::Failure& e) {
+        g_last_error = e.what();
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        g_last_error = "host allocation failed";
+        return CWLB_ERR_OUT_OF_MEMORY;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return CWLB_ERR_RUNTIME;
+    }
+}
+
+void require(bool ok, int code, const char* msg) {
+    if (!ok) cwlb::fail(code, msg);
+}
+
+void check_ctx(cwlb_ctx* ctx) {
+    require(ctx != nullptr, CWLB_ERR_INVALID_ARGUMENT, "null context");
+    CWLB_CUDA(cudaSetDevice(ctx->device));
+}
+
+template <typename T>
+T* stage_h2d(cwlb_ctx* ctx, cwlb::DeviceBuffer& buf, const T* host, size_t count) {
+    T* d = buf.as<T>(count);
+    if (count) CWLB_CUDA(cudaMemcpyAsync(d, host, sizeof(T) * count, cudaMemcpyHostToDevice, ctx->stream));
+    return d;
+}
+
+uint32_t take_device_errors(cwlb_ctx* ctx) {
+    uint32_t flags = 0;
+    CWLB_CUDA(cudaMemcpyAsync(&flags, ctx->d_error_flags, sizeof(flags), cudaMemcpyDeviceToHost,
+                              ctx->stream));
+    CWLB_CUDA(cudaMemsetAsync(ctx->d_error_flags, 0, sizeof(uint32_t), ctx->stream));
+    CWLB_CUDA(cudaStreamSynchronize(ctx->stream));
+    return flags;
+}
+
+void raise_device_errors(uint32_t flags) {
+    if (!flags) return;
+    std::string m = "invalid input detected on the device:";
+    if (flags & CWLB_DEVERR_COL_RANGE) m += " column index outside [0, H.rows());";
+    if (flags & CWLB_DEVERR_ROW_RANGE) m += " task row outside [0, rows);";
+    if (flags & CWLB_DEVERR_OFFSETS) m += " row offsets not monotone or beyond nnz;";
+    if (flags & CWLB_DEVERR_ORIGIN_RANGE) m += " Origin_local id outside [0, rows);";
+    cwlb::fail(CWLB_ERR_INVALID_ARGUMENT, m);
+}
+
+// Shared body of cwlb_spmm_kernel / cwlb_spmm_kernel_large_k.
+void spmm_host(cwlb_ctx* ctx, bool large_k, int32_t n_rows, int32_t nnz,
+               const int32_t* row_offset, const int32_t* col_ind, const float* value,
+               const int32_t* origin, const float* H, int64_t h_rows, int64_t K,
+               int32_t local_dimension, const cwlb_task* tasks, int64_t n_tasks, float* out,
+               double* time_us) {
+    check_ctx(ctx);
+    require(time_us != nullptr, CWLB_ERR_INVALID_ARGUMENT, "null time output");
+    require(n_rows >= 0 && nnz >= 0 && h_rows >= 0 && K >= 0 && n_tasks >= 0,
+            CWLB_ERR_INVALID_ARGUMENT, "negative size");
+    const int64_t max_wg = ctx->props.maxThreadsPerBlock;
+    const size_t out_count = static_cast<size_t>(n_rows) * static_cast<size_t>(K);
+    if (!large_k) {
+        // spmmKernel: K == 0 first, then the work-group limit, then empty tasks
+        // (src/parallelMatrix.cpp:80-104).
+        if (K == 0) {
+            *time_us = 0.0;
+            return;
+        }
+        if (K > max_wg) {
+            cwlb::fail(CWLB_ERR_INVALID_ARGUMENT,
+                       "spmmKernel supports only K <= device max work-group size; "
+                       "use spmmKernelLargeKFallback for larger K.");
+        }
+    } else {
+        // spmmKernelLargeKFallback (src/parallelMatrix.cpp:283-294).
+        if (K <= max_wg) {
+            cwlb::fail(CWLB_ERR_INVALID_ARGUMENT,
+                       "spmmKernelLargeKFallback requires K > device max work-group size.");
+        }
+    }
+    if (n_tasks == 0) {
+        if (out_count) std::memset(out, 0, sizeof(float) * out_count);
+        *time_us = 0.0;
+        return;
+    }
+    // The reference sizes its local-memory tile from local_dimension; a
+    // non-positive tile cannot make progress there, so it is rejected here.
+    if (!large_k) {
+        require(local_dimension > 0, CWLB_ERR_INVALID_ARGUMENT,
+                "local_dimension must be positive");
+    }
+    require(row_offset && origin && tasks && out && (nnz == 0 || (col_ind && value)) &&
+                (h_rows * K == 0 || H),
+            CWLB_ERR_INVALID_ARGUMENT, "null input pointer");
+
+    const int32_t* d_ro = stage_h2d(ctx, ctx->in_rowoff, row_offset, static_cast<size_t>(n_rows) + 1);
+    const int32_t* d_col = stage_h2d(ctx, ctx->in_col, col_ind, static_cast<size_t>(nnz));
+    const float* d_val = stage_h2d(ctx, ctx->in_val, value, static_cast<size_t>(nnz));
+    const int32_t* d_org = stage_h2d(ctx, ctx->in_origin, origin, static_cast<size_t>(n_rows));
+    const float* d_H = stage_h2d(ctx, ctx->in_H, H, static_cast<size_t>(h_rows) * K);
+    const cwlb_task* d_tasks = stage_h2d(ctx, ctx->in_tasks, tasks, static_cast<size_t>(n_tasks));
+    float* d_out = ctx->out_buf.as<float>(out_count);
+
+    CWLB_CUDA(cudaEventRecord(ctx->ev_start, ctx->stream));
+    cwlb::launch_spmm_mean(ctx, n_rows, nnz, d_ro, d_col, d_val, d_org, d_H, h_rows, K, d_tasks,
+                           n_tasks, d_out, 0u);
+    CWLB_CUDA(cudaEventRecord(ctx->ev_stop, ctx->stream));
+    if (out_count) {
+        CWLB_CUDA(cudaMemcpyAsync(out, d_out, sizeof(float) * out_count, cudaMemcpyDeviceToHost,
+                                  ctx->stream));
+    }
+    raise_device_errors(take_device_errors(ctx));
+    float ms = 0.0f;
+    CWLB_CUDA(cudaEventElapsedTime(&ms, ctx->ev_start, ctx->ev_stop));
+    *time_us = static_cast<double>(ms) * 1e3;
+}
+
+cwlb_costs zero_costs() {
+    cwlb_costs c{};
+    return c;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* cwlb_last_error(void) { return g_last_error.c_str(); }
+
+const char* cwlb_version(void) { return "cwlb-spmm-b200 0.1.0 (sm_100a)"; }
+
+int cwlb_ctx_create(int device, cwlb_ctx** out) {
+    return guarded([&] {
+        require(out != nullptr, CWLB_ERR_INVALID_ARGUMENT, "null output");
+        *out = nullptr;
+        int n = 0;
+        if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            cwlb::fail(CWLB_ERR_NO_DEVICE, "no CUDA device available");
+        }
+        require(device >= 0 && device < n, CWLB_ERR_NO_DEVICE, "device index out of range");
+        auto* ctx = new cwlb_ctx();
+        try {
+            ctx->device = device;
+            CWLB_CUDA(cudaSetDevice(device));
+            CWLB_CUDA(cudaGetDeviceProperties(&ctx->props, device));
+            if (ctx->props.major < 10) {
+                cwlb::fail(CWLB_ERR_NO_DEVICE,
+                           "libcwlb_spmm is built for sm_100a (B200); device " +
+                               std::string(ctx->props.name) + " is not compute capability 10.x");
+            }
+            CWLB_CUDA(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
+            ctx->own_stream = true;
+            CWLB_CUDA(cudaEventCreate(&ctx->ev_start));
+            CWLB_CUDA(cudaEventCreate(&ctx->ev_stop));
+            CWLB_CUDA(cudaMalloc(&ctx->d_error_flags, sizeof(uint32_t)));
+            CWLB_CUDA(cudaMemset(ctx->d_error_flags, 0, sizeof(uint32_t)));
+        } catch (...) {
+            cwlb_ctx_destroy(ctx);
+            throw;
+        }
+        *out = ctx;
+    });
+}
+
+int cwlb_ctx_destroy(cwlb_ctx* ctx) {
+    if (!ctx) return CWLB_OK;
+    return guarded([&] {
+        cudaSetDevice(ctx->device);
+        if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+        for (cwlb::DeviceBuffer* b : {&ctx->in_rowoff, &ctx->in_col, &ctx->in_val, &ctx->in_origin,
+                                      &ctx->in_H, &ctx->in_tasks, &ctx->out_buf, &ctx->sort_scratch,
+                                      &ctx->part_scratch, &ctx->part_desc, &ctx->part_tasks,
+                                      &ctx->check_scratch})
+            b->release();
+        if (ctx->d_error_flags) cudaFree(ctx->d_error_flags);
+        if (ctx->ev_start) cudaEventDestroy(ctx->ev_start);
+        if (ctx->ev_stop) cudaEventDestroy(ctx->ev_stop);
+        if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
+        delete ctx;
+    });
+}
+
+int cwlb_ctx_set_stream(cwlb_ctx* ctx, void* stream) {
+    return guarded([&] {
+        check_ctx(ctx);
+        if (ctx->own_stream && ctx->stream) {
+            CWLB_CUDA(cudaStreamSynchronize(ctx->stream));
+            CWLB_CUDA(cudaStreamDestroy(ctx->stream));
+        }
+        ctx->stream = static_cast<cudaStream_t>(stream);
+        ctx->own_stream = false;
+    });
+}
+
+void* cwlb_ctx_stream(cwlb_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+int cwlb_ctx_synchronize(cwlb_ctx* ctx) {
+    return guarded([&] {
+        check_ctx(ctx);
+        CWLB_CUDA(cudaStreamSynchronize(ctx->stream));
+    });
+}
+
+int cwlb_ctx_take_device_errors(cwlb_ctx* ctx, uint32_t* flags) {
+    return guarded([&] {
+        check_ctx(ctx);
+        require(flags != nullptr, CWLB_ERR_INVALID_ARGUMENT, "null output");
+        *flags = take_device_errors(ctx);
+    });
+}
+
+int cwlb_device_info(cwlb_ctx* ctx, int64_t* max_wg, int32_t* cus, int64_t* local_mem,
+                     char* name, size_t name_cap) {
+    return guarded([&] {
+        check_ctx(ctx);
+        if (max_wg) *max_wg = ctx->props.maxThreadsPerBlock;
+        if (cus) *cus = ctx->props.multiProcessorCount;
+        if (local_mem) *local_mem = static_cast<int64_t>(ctx->props.sharedMemPerBlock);
+        if (name && name_cap) {
+            std::strncpy(name, ctx->props.name, name_cap - 1);
+            name[name_cap - 1] = '\0';
+        }
+    });
+}
+
+int cwlb_spmm_kernel(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* row_offset,
+                     const int32_t* col_ind, const float* value, const int32_t* origin_local,
+                     const float* H, int64_t h_rows, int64_t K, int32_t dim_hint,
+                     int32_t local_dimension, const cwlb_task* tasks, int64_t n_tasks,
+                     float* out, double* time_us) {
+    (void)dim_hint;
+    return guarded([&] {
+        spmm_host(ctx, false, n_rows, nnz, row_offset, col_ind, value, origin_local, H, h_rows,
+                  K, local_dimension, tasks, n_tasks, out, time_us);
+    });
+}
+
+int cwlb_spmm_kernel_large_k(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
+                             const int32_t* row_offset, const int32_t* col_ind,
+                             const float* value, const int32_t* origin_local, const float* H,
+                             int64_t h_rows, int64_t K, int32_t dim_hint,
+                             int32_t local_dimension, const cwlb_task* tasks, int64_t n_tasks,
+                             float* out, double* time_us) {
+    (void)dim_hint;
+    return guarded([&] {
+        spmm_host(ctx, true, n_rows, nnz, row_offset, col_ind, value, origin_local, H, h_rows,
+                  K, local_dimension, tasks, n_tasks, out, time_us);
+    });
+}
+
+int cwlb_spmm_mean_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
+                          const int32_t* d_row_offset, const int32_t* d_col_ind,
+                          const float* d_value, const int32_t* d_origin_local, const float* d_H,
+                          int64_t h_rows, int64_t K, const cwlb_task* d_tasks, int64_t n_tasks,
+                          float* d_out, uint32_t flags) {
+    return guarded([&] {
+        check_ctx(ctx);
+        require(n_rows >= 0 && nnz >= 0 && h_rows >= 0 && K >= 0 && n_tasks >= 0,
+                CWLB_ERR_INVALID_ARGUMENT, "negative size");
+        cwlb::launch_spmm_mean(ctx, n_rows, nnz, d_row_offset, d_col_ind, d_value,
+                               d_origin_local, d_H, h_rows, K, d_tasks, n_tasks, d_out, flags);
+    });
+}
+
+int cwlb_tasks_check(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* d_row_offset,
+                     const cwlb_task* d_tasks, int64_t n_tasks, int64_t* bad_tasks,
+                     int64_t* uncovered_rows, int64_t* nnz_coverage_errors) {
+    return guarded([&] {
+        check_ctx(ctx);
+        require(bad_tasks && uncovered_rows && nnz_coverage_errors, CWLB_ERR_INVALID_ARGUMENT,
+                "null output");
+        cwlb::run_tasks_check(ctx, n_rows, nnz, d_row_offset, d_tasks, n_tasks, bad_tasks,
+                              uncovered_rows, nnz_coverage_errors);
+    });
+}
+
+int cwlb_sort_by_degree(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* row_offset,
+                        const int32_t* col_ind, const float* value, int32_t* origin_local,
+                        int32_t* sorted_row_offset, int32_t* sorted_col_ind,
+                        float* sorted_value) {
+    return guarded([&] {
+        check_ctx(ctx);
+        require(n_rows >= 0 && nnz >= 0, CWLB_ERR_INVALID_ARGUMENT, "negative size");
+        if (n_rows == 0) return;  // the reference returns an empty CSR_Order
+        require(row_offset[n_rows] == nnz, CWLB_ERR_RUNTIME,
+                "DPL CPU degree reordering produced an inconsistent NNZ count.");
+        const int32_t* d_ro = stage_h2d(ctx, ctx->in_rowoff, row_offset, static_cast<size_t>(n_rows) + 1);
+        const int32_t* d_col = stage_h2d(ctx, ctx->in_col, col_ind, static_cast<size_t>(nnz));
+        const float* d_val = stage_h2d(ctx, ctx->in_val, value, static_cast<size_t>(nnz));
+        // Outputs staged in out_buf: origin | offsets | cols | values.
+        const size_t n = static_cast<size_t>(n_rows);
+        char* o = static_cast<char*>(ctx->out_buf.ensure(4 * (n + n + 1) + 8 * static_cast<size_t>(nnz) + 64));
+        int32_t* d_org = reinterpret_cast<int32_t*>(o);
+        int32_t* d_nro = d_org + n;
+        int32_t* d_ncol = d_nro + n + 1;
+        float* d_nval = reinterpret_cast<float*>(d_ncol + nnz);
+        cwlb::launch_sort_by_degree(ctx, n_rows, nnz, d_ro, d_col, d_val, d_org, d_nro, d_ncol, d_nval);
+        cudaStream_t s = ctx->stream;
+        CWLB_CUDA(cudaMemcpyAsync(origin_local, d_org, 4 * n, cudaMemcpyDeviceToHost, s));
+        CWLB_CUDA(cudaMemcpyAsync(sorted_row_offset, d_nro, 4 * (n + 1), cudaMemcpyDeviceToHost, s));
+        if (nnz) {
+            CWLB_CUDA(cudaMemcpyAsync(sorted_col_ind, d_ncol, 4 * static_cast<size_t>(nnz), cudaMemcpyDeviceToHost, s));
+            CWLB_CUDA(cudaMemcpyAsync(sorted_value, d_nval, 4 * static_cast<size_t>(nnz), cudaMemcpyDeviceToHost, s));
+        }
+        CWLB_CUDA(cudaStreamSynchronize(s));
+        require(sorted_row_offset[n_rows] == nnz, CWLB_ERR_RUNTIME,
+                "DPL CPU degree reordering produced an inconsistent NNZ count.");
+    });
+}
+
+int cwlb_sort_by_degree_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
+                               const int32_t* d_row_offset, const int32_t* d_col_ind,
+                               const float* d_value, int32_t* d_origin_local,
+                               int32_t* d_sorted_row_offset, int32_t* d_sorted_col_ind,
+                               float* d_sorted_value) {
+    return guarded([&] {
+        check_ctx(ctx);
+        require(n_rows >= 0 && nnz >= 0, CWLB_ERR_INVALID_ARGUMENT, "negative size");
+        if (n_rows == 0) return;
+        cwlb::launch_sort_by_degree(ctx, n_rows, nnz, d_row_offset, d_col_ind, d_value,
+                                    d_origin_local, d_sorted_row_offset, d_sorted_col_ind,
+                                    d_sorted_value);
+    });
+}
+
+int cwlb_partition(cwlb_ctx* ctx, int32_t n_rows, const int32_t* row_offset,
+                   const cwlb_costs* costs, double capacity, cwlb_task* tasks,
+                   int64_t max_tasks, int64_t* n_tasks) {
+    return guarded([&] {
+        check_ctx(ctx);
+        require(costs && n_tasks, CWLB_ERR_INVALID_ARGUMENT, "null argument");
+        *n_tasks = 0;
+        if (n_rows <= 0) return;
+        const int32_t* d_ro = stage_h2d(ctx, ctx->in_rowoff, row_offset, static_cast<size_t>(n_rows) + 1);
+        const int64_t cnt = cwlb::run_partition(ctx, n_rows, d_ro, *costs, capacity);
+        *n_tasks = cnt;
+        if (!tasks) return;
+        if (max_tasks < cnt) {
+            cwlb::fail(CWLB_ERR_BUFFER_TOO_SMALL, "task buffer too small");
+        }
+        if (cnt) {
+            CWLB_CUDA(cudaMemcpyAsync(tasks, ctx->part_tasks.ptr, sizeof(cwlb_task) * cnt,
+                                      cudaMemcpyDeviceToHost, ctx->stream));
+        }
+        CWLB_CUDA(cudaStreamSynchronize(ctx->stream));
+    });
+}
+
+int cwlb_partition_device(cwlb_ctx* ctx, int32_t n_rows, const int32_t* d_row_offset,
+                          const cwlb_costs* costs, double capacity, cwlb_task** d_tasks,
+                          int64_t* n_tasks) {
+    return guarded([&] {
+        check_ctx(ctx);
+        require(costs && d_tasks && n_tasks, CWLB_ERR_INVALID_ARGUMENT, "null argument");
+        *n_tasks = 0;
+        *d_tasks = nullptr;
+        if (n_rows <= 0) return;
+        *n_tasks = cwlb::run_partition(ctx, n_rows, d_row_offset, *costs, capacity);
+        *d_tasks = static_cast<cwlb_task*>(ctx->part_tasks.ptr);
+    });
+}
+
+// ---------------------------------------------------------------------------
+// Host-side helpers (scalar arithmetic the reference also does on the host).
+
+double cwlb_capacity_from_s(int32_t s, const cwlb_costs* costs) {
+    const cwlb_costs c = costs ? *costs : zero_costs();
+    const double edge = c.C_compute_ns + c.C_load_ns;
+    const int32_t cs = std::max<int32_t>(1, s);
+    if (edge <= 0.0) return std::max(0.0, c.C_atomic_ns);
+    return std::max(0.0, c.C_atomic_ns + edge * static_cast<double>(cs));
+}
+
+int32_t cwlb_segment_size(const cwlb_costs* costs, double capacity) {
+    const cwlb_costs c = costs ? *costs : zero_costs();
+    const double wCL = c.C_compute_ns + c.C_load_ns;
+    const double q = std::floor((capacity - c.C_atomic_ns) / std::max(1e-30, wCL));
+    // double -> int32 as x86-64 converts it: out-of-range and NaN give INT32_MIN.
+    const int32_t t = (q >= -2147483648.0 && q < 2147483648.0) ? static_cast<int32_t>(q)
+                                                                : std::numeric_limits<int32_t>::min();
+    return std::max<int32_t>(1, t);
+}
+
+int cwlb_wave_based_s(int64_t nnz, int32_t compute_units, int32_t wave, int32_t* s) {
+    return guarded([&] {
+        require(s != nullptr, CWLB_ERR_INVALID_ARGUMENT, "null output");
+        if (compute_units <= 0 || wave <= 0) {
+            cwlb::fail(CWLB_ERR_INVALID_ARGUMENT, "compute_units and wave must be positive.");
+        }
+        const uint64_t n = static_cast<uint64_t>(nnz);
+        const uint64_t d = static_cast<uint64_t>(compute_units) * static_cast<uint64_t>(wave);
+        uint64_t v = (n + d - 1) / d;
+        v = std::max<uint64_t>(1, v);
+        v = std::min<uint64_t>(v, static_cast<uint64_t>(std::numeric_limits<int32_t>::max()));
+        *s = static_cast<int32_t>(v);
+    });
+}
+
+void cwlb_recommended_candidate_w(uint64_t nnz, int32_t out[3]) {
+    // nnz thresholds and the leading candidate of each band; the other two
+    // candidates halve it (main.cpp:87-95).
+    static const uint64_t limit[] = {100000ULL, 500000ULL, 1000000ULL, 5000000ULL,
+                                     10000000ULL, 50000000ULL};
+    static const int32_t lead[] = {64, 128, 256, 512, 1024, 4096, 8192};
+    int i = 0;
+    while (i < 6 && nnz >= limit[i]) ++i;
+    out[0] = lead[i];
+    out[1] = lead[i] / 2;
+    out[2] = lead[i] / 4;
+}
+
+int cwlb_save_costs(const cwlb_costs* costs, const char* path, int32_t append,
+                    int32_t precision) {
+    namespace fs = std::filesystem;
+    if (!costs || !path || !*path) {
+        g_last_error = "empty cost-file path";
+        return CWLB_ERR_RUNTIME;
+    }
+    std::error_code ec;
+    const fs::path p(path);
+    if (p.has_parent_path()) {
+        const fs::path dir = p.parent_path();
+        if (fs::exists(dir, ec) && !fs::is_directory(dir, ec)) {
+            g_last_error = "cost-file parent is not a directory";
+            return CWLB_ERR_RUNTIME;
+        }
+        if (!fs::exists(dir, ec) && !fs::create_directories(dir, ec) && ec) {
+            g_last_error = "cannot create the cost-file directory";
+            return CWLB_ERR_RUNTIME;
+        }
+    }
+    std::ofstream ofs(p, std::ios::out | (append ? std::ios::app : std::ios::trunc));
+    if (!ofs.is_open()) {
+        g_last_error = "cannot open the cost file";
+        return CWLB_ERR_RUNTIME;
+    }
+    ofs << std::fixed << std::setprecision(precision) << costs->C_compute_ns << "\n"
+        << costs->C_load_ns << "\n"
+        << costs->C_store_ns << "\n"
+        << costs->C_atomic_ns << "\n";
+    if (!ofs.good()) {
+        g_last_error = "cost-file write failed";
+        return CWLB_ERR_RUNTIME;
+    }
+    return CWLB_OK;
+}
+
+int cwlb_read_costs(cwlb_costs* costs, const char* path) {
+    if (!costs || !path) {
+        g_last_error = "null argument";
+        return CWLB_ERR_INVALID_ARGUMENT;
+    }
+    std::ifstream ifs(path);
+    double v[4];
+    if (!ifs.is_open() || !(ifs >> v[0]) || !(ifs >> v[1]) || !(ifs >> v[2]) || !(ifs >> v[3])) {
+        g_last_error = std::string("cannot read microbenchmark cost file: ") + path;
+        return CWLB_ERR_RUNTIME;
+    }
+    costs->C_compute_ns = v[0];
+    costs->C_load_ns = v[1];
+    costs->C_store_ns = v[2];
+    costs->C_atomic_ns = v[3];
+    return CWLB_OK;
+}
+
+}  // extern "C"

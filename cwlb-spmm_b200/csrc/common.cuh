@@ -1,0 +1,92 @@
+// Internal helpers shared by the CUDA translation units of libcwlb_spmm.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "cwlb_spmm.h"
+
+namespace cwlb {
+
+// Library-internal failure carrying a cwlb_status; converted to a return code
+// (and a thread-local message) at the C boundary.
+struct Failure : std::runtime_error {
+    int code;
+    Failure(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+[[noreturn]] inline void fail(int code, const std::string& msg) { throw Failure(code, msg); }
+
+inline void check_cuda(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return;
+    if (e == cudaErrorMemoryAllocation) {
+        fail(CWLB_ERR_OUT_OF_MEMORY, std::string(what) + ": " + cudaGetErrorString(e));
+    }
+    fail(CWLB_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define CWLB_CUDA(call) ::cwlb::check_cuda((call), #call)
+#define CWLB_LAUNCH_CHECK(name) ::cwlb::check_cuda(cudaGetLastError(), name)
+
+// A device buffer that grows on demand and is reused across calls.
+struct DeviceBuffer {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    void* ensure(size_t need) {
+        if (need <= bytes) return ptr;
+        release();
+        size_t want = need < 256 ? 256 : need;
+        CWLB_CUDA(cudaMalloc(&ptr, want));
+        bytes = want;
+        return ptr;
+    }
+    template <typename T>
+    T* as(size_t count) {
+        return static_cast<T*>(ensure(count * sizeof(T)));
+    }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+};
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace cwlb
+
+// The context (opaque in the C API).
+struct cwlb_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    cudaDeviceProp props{};
+    cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
+    uint32_t* d_error_flags = nullptr;  // CWLB_DEVERR_* bits raised by kernels
+    // Scratch for the host-buffer entry points (inputs/outputs staged on the
+    // device) and for the sort / partition pipelines.
+    cwlb::DeviceBuffer in_rowoff, in_col, in_val, in_origin, in_H, in_tasks, out_buf;
+    cwlb::DeviceBuffer sort_scratch, part_scratch, part_desc, part_tasks, check_scratch;
+};
+
+namespace cwlb {
+
+// Launchers implemented in the .cu files (all asynchronous on ctx->stream).
+void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
+                      const int32_t* col, const float* val, const int32_t* origin,
+                      const float* H, int64_t h_rows, int64_t K, const cwlb_task* tasks,
+                      int64_t n_tasks, float* out, uint32_t flags);
+void run_tasks_check(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
+                     const cwlb_task* tasks, int64_t n_tasks, int64_t* bad_tasks,
+                     int64_t* uncovered_rows, int64_t* nnz_errors);
+void launch_sort_by_degree(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
+                           const int32_t* col, const float* val, int32_t* origin,
+                           int32_t* new_rowoff, int32_t* new_col, float* new_val);
+// Returns the number of tasks; the tasks are in ctx->part_tasks.
+int64_t run_partition(cwlb_ctx* ctx, int32_t n_rows, const int32_t* d_rowoff,
+                      const cwlb_costs& costs, double capacity);
+
+}  // namespace cwlb

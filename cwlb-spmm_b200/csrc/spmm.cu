@@ -1,0 +1,569 @@
+// Mean-aggregation SpMM over cost-weighted tasks (sm_100a).
+//
+// Semantics follow spmmKernel / spmmKernelLargeKFallback
+// (src/parallelMatrix.cpp:151-236 and :411-664 of the reference): for every
+// task and every reordered row r it covers, the fragment [begin, end) of row r
+// (begin = first_row_offset on the task's first row, end = last_row_nnz on its
+// last row when > 0, both clamped to [0, deg]) is accumulated as
+// acc = fma(value, H[col][k], acc) in nnz order, divided by the FULL degree,
+// and stored to out[origin[r]][k] if the fragment is the whole row, or added
+// atomically otherwise.
+//
+// B200 mapping (the reference instead gives each task a work-group of K
+// work-items and stages the CSR fragment through local memory):
+//   * one warp per task, 8 warps per CTA; the hardware block scheduler
+//     balances the cost-equalised tasks across the 148 SMs;
+//   * the warp is split into G = 32/L lane groups of L lanes; each lane owns V
+//     float4 columns of the row (128-bit coalesced gathers of H rows), so a
+//     K-wide row is covered by L*V float4 and K > 4*L*V is tiled over
+//     blockIdx.y;
+//   * tasks with several rows give each group its own row (rows inside a task
+//     have near-equal degree because rows are degree-sorted); a single-row
+//     task (a long-row fragment) splits its nonzeros over the groups and
+//     reduces them with warp shuffles;
+//   * U nonzeros are gathered per step so that U*V independent 16-byte loads
+//     are in flight per lane before their FMAs; per column the FMA chain
+//     keeps nnz order, so whole rows handled by one group round exactly as
+//     the reference does;
+//   * 1/deg is applied in registers before the single write-back: streaming
+//     stores for whole rows, red.global.add.v4.f32 for fragments.
+// No tensor cores: the operation is a gather (each nonzero reads a different
+// H row), bound by memory, not by a dense contraction.
+//
+// Safety: indices are checked before use.  A column outside [0, h_rows), a
+// task row outside [0, n_rows), non-monotone offsets or an origin outside
+// [0, n_rows) never fault: the entry is skipped and a CWLB_DEVERR_* bit is
+// raised in the context's device error word.
+#include "common.cuh"
+
+namespace cwlb {
+namespace {
+
+constexpr int kWarpsPerCta = 8;
+constexpr int kThreads = kWarpsPerCta * 32;
+
+struct SpmmArgs {
+    const int32_t* __restrict__ rowoff;
+    const int32_t* __restrict__ col;
+    const float* __restrict__ val;
+    const int32_t* __restrict__ origin;
+    const float* __restrict__ H;
+    const cwlb_task* __restrict__ tasks;
+    float* __restrict__ out;
+    uint32_t* err;
+    int64_t h_rows;
+    int64_t K;  // row stride (in floats) of H and out
+    int64_t n_tasks;
+    int32_t n_rows;
+    int32_t nnz;
+    int32_t write_empty;  // rows-covered mode: degree-0 rows get explicit zeros
+};
+
+__device__ __forceinline__ void raise_err(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
+
+__device__ __forceinline__ float4 fma4(float a, const float4& x, const float4& acc) {
+    return make_float4(fmaf(a, x.x, acc.x), fmaf(a, x.y, acc.y), fmaf(a, x.z, acc.z),
+                       fmaf(a, x.w, acc.w));
+}
+
+__device__ __forceinline__ float4 div4(const float4& a, float d) {
+    return make_float4(__fdiv_rn(a.x, d), __fdiv_rn(a.y, d), __fdiv_rn(a.z, d),
+                       __fdiv_rn(a.w, d));
+}
+
+// Row bookkeeping shared by all kernels.  Returns false when the row has no
+// fragment to process (after writing zeros for an empty row if requested).
+struct RowFrag {
+    int32_t base;   // rowoff[r]
+    int32_t deg;
+    int32_t begin;  // fragment within the row
+    int32_t end;
+    int32_t orig;
+};
+
+__device__ __forceinline__ int row_fragment(const SpmmArgs& a, int r, const cwlb_task& t,
+                                            RowFrag& f) {
+    // 0: process, 1: empty row (deg <= 0), 2: nothing to do / invalid
+    const int32_t b0 = __ldg(a.rowoff + r);
+    const int32_t b1 = __ldg(a.rowoff + r + 1);
+    if (b0 < 0 || b1 < b0 || b1 > a.nnz) {
+        raise_err(a.err, CWLB_DEVERR_OFFSETS);
+        return 2;
+    }
+    f.orig = __ldg(a.origin + r);
+    if (f.orig < 0 || f.orig >= a.n_rows) {
+        raise_err(a.err, CWLB_DEVERR_ORIGIN_RANGE);
+        return 2;
+    }
+    f.base = b0;
+    f.deg = b1 - b0;
+    if (f.deg <= 0) return 1;
+    int32_t begin = (r == t.row_start) ? t.first_row_offset : 0;
+    int32_t end = f.deg;
+    if (r == t.row_end - 1 && t.last_row_nnz > 0) end = t.last_row_nnz;
+    begin = min(max(begin, 0), f.deg);
+    end = min(max(end, begin), f.deg);
+    f.begin = begin;
+    f.end = end;
+    return begin < end ? 0 : 2;
+}
+
+__device__ __forceinline__ bool load_task(const SpmmArgs& a, int64_t t, cwlb_task& tk) {
+    const int4 raw = __ldg(reinterpret_cast<const int4*>(a.tasks) + t);
+    tk.row_start = raw.x;
+    tk.row_end = raw.y;
+    tk.first_row_offset = raw.z;
+    tk.last_row_nnz = raw.w;
+    if (tk.row_start < 0 || tk.row_end > a.n_rows || tk.row_start > tk.row_end) {
+        raise_err(a.err, CWLB_DEVERR_ROW_RANGE);
+        return false;
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------------------
+// float4 kernel: L lanes per group, V float4 per lane, U nonzeros per step.
+
+template <int L, int V>
+struct VecCfg {
+    static constexpr int G = 32 / L;
+    static constexpr int U = V == 1 ? 8 : (V == 2 ? 4 : 2);
+};
+
+// Gather-accumulate nonzeros j = j0, j0 + step, ... < j1 into acc (per column
+// the FMA chain follows increasing j).
+template <int L, int V>
+__device__ __forceinline__ void gather_accumulate(const SpmmArgs& a, int32_t j0, int32_t j1,
+                                                  int32_t step, const int64_t (&q)[V],
+                                                  const bool (&ok)[V], float4 (&acc)[V]) {
+    constexpr int U = VecCfg<L, V>::U;
+    const float4* __restrict__ H4 = reinterpret_cast<const float4*>(a.H);
+    const int64_t K4 = a.K >> 2;
+    int32_t j = j0;
+    for (; j + (U - 1) * step < j1; j += U * step) {
+        int32_t c[U];
+        float v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            c[u] = __ldg(a.col + j + u * step);
+            v[u] = __ldg(a.val + j + u * step);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (static_cast<uint64_t>(c[u]) >= static_cast<uint64_t>(a.h_rows)) {
+                raise_err(a.err, CWLB_DEVERR_COL_RANGE);
+                c[u] = 0;
+                v[u] = 0.0f;
+            }
+        }
+        float4 x[U][V];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                x[u][i] = ok[i] ? __ldg(H4 + static_cast<int64_t>(c[u]) * K4 + q[i])
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) acc[i] = fma4(v[u], x[u][i], acc[i]);
+        }
+    }
+    for (; j < j1; j += step) {
+        int32_t c = __ldg(a.col + j);
+        float v = __ldg(a.val + j);
+        if (static_cast<uint64_t>(c) >= static_cast<uint64_t>(a.h_rows)) {
+            raise_err(a.err, CWLB_DEVERR_COL_RANGE);
+            c = 0;
+            v = 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            const float4 x = ok[i] ? __ldg(H4 + static_cast<int64_t>(c) * K4 + q[i])
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            acc[i] = fma4(v, x, acc[i]);
+        }
+    }
+}
+
+template <int V>
+__device__ __forceinline__ void write_row(const SpmmArgs& a, const RowFrag& f,
+                                          const int64_t (&q)[V], const bool (&ok)[V],
+                                          float4 (&acc)[V]) {
+    float4* out4 = reinterpret_cast<float4*>(a.out) + static_cast<int64_t>(f.orig) * (a.K >> 2);
+    const float d = static_cast<float>(f.deg);
+    const bool full = f.begin == 0 && f.end == f.deg;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        if (!ok[i]) continue;
+        const float4 r = div4(acc[i], d);
+        if (full) {
+            __stcs(out4 + q[i], r);
+        } else {
+            atomicAdd(out4 + q[i], r);
+        }
+    }
+}
+
+template <int L, int V>
+__global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
+    constexpr int G = VecCfg<L, V>::G;
+    const int lane = threadIdx.x & 31;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
+    if (t >= a.n_tasks) return;
+    cwlb_task tk;
+    if (!load_task(a, t, tk)) return;
+
+    const int g = lane / L;
+    const int lg = lane % L;
+    const int64_t K4 = a.K >> 2;
+    const int64_t q0 = static_cast<int64_t>(blockIdx.y) * (L * V);
+    int64_t q[V];
+    bool ok[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        q[i] = q0 + lg + i * L;
+        ok[i] = q[i] < K4;
+    }
+    const int n_task_rows = tk.row_end - tk.row_start;
+
+    if (G == 1 || n_task_rows != 1) {
+        // Each group takes its own rows; nnz order within a row is preserved.
+        for (int r = tk.row_start + g; r < tk.row_end; r += G) {
+            RowFrag f;
+            const int st = row_fragment(a, r, tk, f);
+            if (st == 1) {
+                if (a.write_empty) {
+                    float4* out4 = reinterpret_cast<float4*>(a.out) +
+                                   static_cast<int64_t>(f.orig) * K4;
+#pragma unroll
+                    for (int i = 0; i < V; ++i)
+                        if (ok[i]) __stcs(out4 + q[i], make_float4(0.f, 0.f, 0.f, 0.f));
+                }
+                continue;
+            }
+            if (st != 0) continue;
+            float4 acc[V];
+#pragma unroll
+            for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            gather_accumulate<L, V>(a, f.base + f.begin, f.base + f.end, 1, q, ok, acc);
+            write_row<V>(a, f, q, ok, acc);
+        }
+    } else {
+        // One row: the G groups split its nonzeros, then reduce by shuffles.
+        const int r = tk.row_start;
+        RowFrag f;
+        const int st = row_fragment(a, r, tk, f);
+        if (st == 1) {
+            if (a.write_empty && g == 0) {
+                float4* out4 = reinterpret_cast<float4*>(a.out) + static_cast<int64_t>(f.orig) * K4;
+#pragma unroll
+                for (int i = 0; i < V; ++i)
+                    if (ok[i]) __stcs(out4 + q[i], make_float4(0.f, 0.f, 0.f, 0.f));
+            }
+            return;
+        }
+        if (st != 0) return;
+        float4 acc[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        gather_accumulate<L, V>(a, f.base + f.begin + g, f.base + f.end, G, q, ok, acc);
+#pragma unroll
+        for (int s = L; s < 32; s <<= 1) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                acc[i].x += __shfl_xor_sync(0xffffffffu, acc[i].x, s);
+                acc[i].y += __shfl_xor_sync(0xffffffffu, acc[i].y, s);
+                acc[i].z += __shfl_xor_sync(0xffffffffu, acc[i].z, s);
+                acc[i].w += __shfl_xor_sync(0xffffffffu, acc[i].w, s);
+            }
+        }
+        if (g == 0) write_row<V>(a, f, q, ok, acc);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Scalar kernel for K not a multiple of 4 or unaligned H / out: one warp per
+// task, lane k owns columns k0 + lane + 32*i, rows in sequence.
+
+template <int V>
+__global__ void __launch_bounds__(kThreads) spmm_scalar_kernel(SpmmArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
+    if (t >= a.n_tasks) return;
+    cwlb_task tk;
+    if (!load_task(a, t, tk)) return;
+    const int64_t k0 = static_cast<int64_t>(blockIdx.y) * (32 * V);
+    int64_t kk[V];
+    bool ok[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        kk[i] = k0 + lane + 32 * i;
+        ok[i] = kk[i] < a.K;
+    }
+    for (int r = tk.row_start; r < tk.row_end; ++r) {
+        RowFrag f;
+        const int st = row_fragment(a, r, tk, f);
+        float* orow = a.out + static_cast<int64_t>(f.orig) * a.K;
+        if (st == 1) {
+            if (a.write_empty) {
+#pragma unroll
+                for (int i = 0; i < V; ++i)
+                    if (ok[i]) __stcs(orow + kk[i], 0.0f);
+            }
+            continue;
+        }
+        if (st != 0) continue;
+        float acc[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] = 0.0f;
+        for (int32_t j = f.base + f.begin; j < f.base + f.end; ++j) {
+            int32_t c = __ldg(a.col + j);
+            float v = __ldg(a.val + j);
+            if (static_cast<uint64_t>(c) >= static_cast<uint64_t>(a.h_rows)) {
+                raise_err(a.err, CWLB_DEVERR_COL_RANGE);
+                c = 0;
+                v = 0.0f;
+            }
+            const float* hrow = a.H + static_cast<int64_t>(c) * a.K;
+#pragma unroll
+            for (int i = 0; i < V; ++i)
+                acc[i] = fmaf(v, ok[i] ? __ldg(hrow + kk[i]) : 0.0f, acc[i]);
+        }
+        const float d = static_cast<float>(f.deg);
+        const bool full = f.begin == 0 && f.end == f.deg;
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            if (!ok[i]) continue;
+            const float r_ = __fdiv_rn(acc[i], d);
+            if (full) __stcs(orow + kk[i], r_);
+            else atomicAdd(orow + kk[i], r_);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Rows-covered mode: zero exactly the output rows that are assembled from
+// fragments (each such row has one fragment starting at offset 0), before the
+// aggregation kernel adds into them.  One warp per task.
+
+__global__ void __launch_bounds__(kThreads) zero_split_rows_kernel(SpmmArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
+    if (t >= a.n_tasks) return;
+    const int4 raw = __ldg(reinterpret_cast<const int4*>(a.tasks) + t);
+    cwlb_task tk{raw.x, raw.y, raw.z, raw.w};
+    if (tk.row_start < 0 || tk.row_end > a.n_rows || tk.row_start >= tk.row_end) return;
+    const int rows[2] = {tk.row_start, tk.row_end - 1};
+    const int n = rows[0] == rows[1] ? 1 : 2;
+    for (int i = 0; i < n; ++i) {
+        const int r = rows[i];
+        const int32_t b0 = __ldg(a.rowoff + r);
+        const int32_t b1 = __ldg(a.rowoff + r + 1);
+        if (b0 < 0 || b1 < b0 || b1 > a.nnz) continue;
+        const int32_t deg = b1 - b0;
+        if (deg <= 0) continue;
+        int32_t begin = (r == tk.row_start) ? tk.first_row_offset : 0;
+        int32_t end = deg;
+        if (r == tk.row_end - 1 && tk.last_row_nnz > 0) end = tk.last_row_nnz;
+        begin = min(max(begin, 0), deg);
+        end = min(max(end, begin), deg);
+        if (!(begin == 0 && end > 0 && end < deg)) continue;
+        const int32_t o = __ldg(a.origin + r);
+        if (o < 0 || o >= a.n_rows) continue;
+        float* orow = a.out + static_cast<int64_t>(o) * a.K;
+        for (int64_t k = lane; k < a.K; k += 32) orow[k] = 0.0f;
+    }
+}
+
+template <int L, int V>
+void launch_vec(const SpmmArgs& a, cudaStream_t s) {
+    const int64_t K4 = a.K >> 2;
+    const int64_t tiles = ceil_div(K4, L * V);
+    dim3 grid(static_cast<unsigned>(ceil_div(a.n_tasks, kWarpsPerCta)),
+              static_cast<unsigned>(tiles));
+    spmm_vec_kernel<L, V><<<grid, kThreads, 0, s>>>(a);
+}
+
+template <int L>
+void launch_vec_v(int V, const SpmmArgs& a, cudaStream_t s) {
+    switch (V) {
+        case 1: launch_vec<L, 1>(a, s); break;
+        case 2: launch_vec<L, 2>(a, s); break;
+        case 3: launch_vec<L, 3>(a, s); break;
+        default: launch_vec<L, 4>(a, s); break;
+    }
+}
+
+// Picks (L, V) for K4 float4 columns: the least padding, then the widest
+// group (fewest groups per warp).
+void pick_vec_shape(int64_t K4, int& L, int& V) {
+    int64_t best_waste = -1;
+    for (int l = 32; l >= 1; l >>= 1) {
+        for (int v = 1; v <= 4; ++v) {
+            const int64_t span = static_cast<int64_t>(l) * v;
+            // One tile whenever it fits; wider rows use full 128-float4 tiles.
+            if (K4 > 128 ? span != 128 : span < K4) continue;
+            const int64_t tiles = ceil_div(K4, span);
+            const int64_t waste = tiles * span - K4;
+            if (best_waste < 0 || waste < best_waste) {
+                best_waste = waste;
+                L = l;
+                V = v;
+            }
+        }
+    }
+}
+
+}  // namespace
+
+void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
+                      const int32_t* col, const float* val, const int32_t* origin,
+                      const float* H, int64_t h_rows, int64_t K, const cwlb_task* tasks,
+                      int64_t n_tasks, float* out, uint32_t flags) {
+    if (K <= 0 || n_rows <= 0) return;
+    cudaStream_t s = ctx->stream;
+    const bool covered = (flags & CWLB_ROWS_COVERED) != 0;
+    if (!covered) {
+        CWLB_CUDA(cudaMemsetAsync(out, 0, sizeof(float) * static_cast<size_t>(n_rows) * K, s));
+    }
+    if (n_tasks <= 0) return;
+    if (nnz > 0 && h_rows <= 0) fail(CWLB_ERR_INVALID_ARGUMENT, "H has no rows but the CSR has nonzeros");
+
+    SpmmArgs a{};
+    a.rowoff = rowoff;
+    a.col = col;
+    a.val = val;
+    a.origin = origin;
+    a.H = H;
+    a.tasks = tasks;
+    a.out = out;
+    a.err = ctx->d_error_flags;
+    a.h_rows = h_rows;
+    a.K = K;
+    a.n_tasks = n_tasks;
+    a.n_rows = n_rows;
+    a.nnz = nnz;
+    a.write_empty = covered ? 1 : 0;
+
+    if (covered) {
+        dim3 grid(static_cast<unsigned>(ceil_div(n_tasks, kWarpsPerCta)));
+        zero_split_rows_kernel<<<grid, kThreads, 0, s>>>(a);
+        CWLB_LAUNCH_CHECK("zero_split_rows_kernel");
+    }
+
+    const bool aligned = (reinterpret_cast<uintptr_t>(H) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(out) % 16 == 0) && (K % 4 == 0);
+    if (aligned) {
+        int L = 32, V = 1;
+        pick_vec_shape(K >> 2, L, V);
+        switch (L) {
+            case 1: launch_vec_v<1>(V, a, s); break;
+            case 2: launch_vec_v<2>(V, a, s); break;
+            case 4: launch_vec_v<4>(V, a, s); break;
+            case 8: launch_vec_v<8>(V, a, s); break;
+            case 16: launch_vec_v<16>(V, a, s); break;
+            default: launch_vec_v<32>(V, a, s); break;
+        }
+        CWLB_LAUNCH_CHECK("spmm_vec_kernel");
+    } else {
+        const int V = static_cast<int>(std::min<int64_t>(4, ceil_div(K, 32)));
+        dim3 grid(static_cast<unsigned>(ceil_div(n_tasks, kWarpsPerCta)),
+                  static_cast<unsigned>(ceil_div(K, 32 * V)));
+        switch (V) {
+            case 1: spmm_scalar_kernel<1><<<grid, kThreads, 0, s>>>(a); break;
+            case 2: spmm_scalar_kernel<2><<<grid, kThreads, 0, s>>>(a); break;
+            case 3: spmm_scalar_kernel<3><<<grid, kThreads, 0, s>>>(a); break;
+            default: spmm_scalar_kernel<4><<<grid, kThreads, 0, s>>>(a); break;
+        }
+        CWLB_LAUNCH_CHECK("spmm_scalar_kernel");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Task-list validation (cwlb_tasks_check).
+
+namespace {
+
+__global__ void check_tasks_kernel(const int32_t* __restrict__ rowoff, int32_t n_rows,
+                                   int32_t nnz, const cwlb_task* __restrict__ tasks,
+                                   int64_t n_tasks, uint32_t* __restrict__ row_seen,
+                                   uint32_t* __restrict__ nnz_count,
+                                   unsigned long long* __restrict__ bad) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (t >= n_tasks) return;
+    const cwlb_task tk = tasks[t];
+    if (tk.row_start < 0 || tk.row_end > n_rows || tk.row_start > tk.row_end) {
+        if (lane == 0) atomicAdd(bad, 1ull);
+        return;
+    }
+    for (int r = tk.row_start; r < tk.row_end; ++r) {
+        if (lane == 0) row_seen[r] = 1u;
+        const int32_t b0 = rowoff[r], b1 = rowoff[r + 1];
+        if (b0 < 0 || b1 < b0 || b1 > nnz) continue;
+        const int32_t deg = b1 - b0;
+        if (deg <= 0) continue;
+        int32_t begin = (r == tk.row_start) ? tk.first_row_offset : 0;
+        int32_t end = deg;
+        if (r == tk.row_end - 1 && tk.last_row_nnz > 0) end = tk.last_row_nnz;
+        begin = min(max(begin, 0), deg);
+        end = min(max(end, begin), deg);
+        for (int32_t j = b0 + begin + lane; j < b0 + end; j += 32) atomicAdd(nnz_count + j, 1u);
+    }
+}
+
+__global__ void count_coverage_kernel(const uint32_t* __restrict__ row_seen, int32_t n_rows,
+                                      const uint32_t* __restrict__ nnz_count, int32_t nnz,
+                                      unsigned long long* __restrict__ res) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    unsigned long long unc = 0, bad = 0;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n_rows;
+         i += stride)
+        unc += row_seen[i] == 0u;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nnz;
+         i += stride)
+        bad += nnz_count[i] != 1u;
+    for (int o = 16; o > 0; o >>= 1) {
+        unc += __shfl_xor_sync(0xffffffffu, unc, o);
+        bad += __shfl_xor_sync(0xffffffffu, bad, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        if (unc) atomicAdd(res + 0, unc);
+        if (bad) atomicAdd(res + 1, bad);
+    }
+}
+
+}  // namespace
+
+void run_tasks_check(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
+                     const cwlb_task* tasks, int64_t n_tasks, int64_t* bad_tasks,
+                     int64_t* uncovered_rows, int64_t* nnz_errors) {
+    cudaStream_t s = ctx->stream;
+    const size_t rows_b = sizeof(uint32_t) * static_cast<size_t>(n_rows > 0 ? n_rows : 0);
+    const size_t nnz_b = sizeof(uint32_t) * static_cast<size_t>(nnz > 0 ? nnz : 0);
+    char* base = static_cast<char*>(ctx->check_scratch.ensure(rows_b + nnz_b + 64));
+    uint32_t* row_seen = reinterpret_cast<uint32_t*>(base);
+    uint32_t* nnz_count = reinterpret_cast<uint32_t*>(base + rows_b);
+    unsigned long long* res = reinterpret_cast<unsigned long long*>(base + rows_b + nnz_b);
+    CWLB_CUDA(cudaMemsetAsync(base, 0, rows_b + nnz_b + 64, s));
+    if (n_tasks > 0) {
+        const int64_t threads = n_tasks * 32;
+        check_tasks_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(
+            rowoff, n_rows, nnz, tasks, n_tasks, row_seen, nnz_count, res + 2);
+        CWLB_LAUNCH_CHECK("check_tasks_kernel");
+    }
+    count_coverage_kernel<<<ctx->props.multiProcessorCount * 4, 256, 0, s>>>(row_seen, n_rows,
+                                                                          nnz_count, nnz, res);
+    CWLB_LAUNCH_CHECK("count_coverage_kernel");
+    unsigned long long h[3];
+    CWLB_CUDA(cudaMemcpyAsync(h, res, sizeof(h), cudaMemcpyDeviceToHost, s));
+    CWLB_CUDA(cudaStreamSynchronize(s));
+    *uncovered_rows = static_cast<int64_t>(h[0]);
+    *nnz_errors = static_cast<int64_t>(h[1]);
+    *bad_tasks = static_cast<int64_t>(h[2]);
+}
+
+}  // namespace cwlb

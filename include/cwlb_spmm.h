@@ -1,0 +1,219 @@
+/*
+ * cwlb_spmm.h - C ABI of the B200 (sm_100a) CWLB-SpMM library.
+ *
+ * The hot path is FP32 CSR mean aggregation
+ *     out[origin[r], k] = (1 / deg_r) * sum_{j in row r} value_j * H[col_j, k]
+ * over a degree-reordered CSR, driven by cost-weighted task descriptors.
+ * Every entry point below replaces one interface of the reference
+ * (hhx-C/CWLB-SpMM); the comment on each names the reference code by
+ * file:line, relative to that project's root.  The C++17 drop-in API in
+ * cwlb-spmm_b200/host/include/ (Matrix.h, utils.h, parallelMatrix.h, ...)
+ * is a thin layer over these functions.
+ *
+ * Conventions
+ *   - Every function returns a cwlb_status; on failure cwlb_last_error()
+ *     returns the message of the calling thread's last failure.  Status codes
+ *     map one-to-one onto the C++ exception types the reference throws.
+ *   - "host" pointers are ordinary (pageable or pinned) host memory;
+ *     "d_" pointers are device memory of the context's device.
+ *   - *_device entry points are asynchronous on the context's stream; all
+ *     others are synchronous (they return when results are in host memory),
+ *     as the reference's q.wait() based functions are.
+ *   - A context is bound to one device and is not thread-safe; use one
+ *     context per GPU and per host thread.
+ *   - The library owns only its scratch memory; it never frees caller memory.
+ *   - No entry point falls back to a CPU implementation.  Without a usable
+ *     CUDA device cwlb_ctx_create fails with CWLB_ERR_NO_DEVICE.
+ */
+#ifndef CWLB_SPMM_H_
+#define CWLB_SPMM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum cwlb_status {
+    CWLB_OK = 0,
+    CWLB_ERR_INVALID_ARGUMENT = 1, /* reference: std::invalid_argument */
+    CWLB_ERR_RUNTIME = 2,          /* reference: std::runtime_error */
+    CWLB_ERR_OVERFLOW = 3,         /* reference: std::overflow_error */
+    CWLB_ERR_CUDA = 4,             /* a CUDA runtime call failed */
+    CWLB_ERR_NO_DEVICE = 5,        /* no usable CUDA device */
+    CWLB_ERR_BUFFER_TOO_SMALL = 6, /* output capacity too small; size reported */
+    CWLB_ERR_OUT_OF_MEMORY = 7     /* device allocation failed */
+} cwlb_status;
+
+/* ParallelDataWeighted (include/utils.h:15-20): one task = a half-open range
+ * of reordered rows plus the nnz offsets that bound its first and last row. */
+typedef struct cwlb_task {
+    int32_t row_start;        /* first reordered row, inclusive */
+    int32_t row_end;          /* last reordered row, exclusive */
+    int32_t first_row_offset; /* nnz offset within the first row */
+    int32_t last_row_nnz;     /* end offset within the last row; 0 = full degree */
+} cwlb_task;
+
+/* SpmmCostParams (include/utils.h:23-33): calibrated weights (ns x 10 per
+ * operation) plus the calibration metadata. */
+typedef struct cwlb_costs {
+    double C_compute_ns;
+    double C_load_ns;
+    double C_store_ns;
+    double C_atomic_ns;
+    int32_t K;
+    int32_t WI;
+    int32_t repeat;
+    int32_t atomic_writers_per_addr;
+} cwlb_costs;
+
+typedef struct cwlb_ctx cwlb_ctx;
+
+/* Message of the calling thread's last failing call ("" if none). */
+const char* cwlb_last_error(void);
+/* Library version string. */
+const char* cwlb_version(void);
+
+/* ---------------------------------------------------------------- context */
+
+/* Replaces sycl::queue(gpu_selector_v, enable_profiling) (main.cpp:514-516,
+ * weightCost.cpp:44-46): binds CUDA device `device` and creates a stream. */
+int cwlb_ctx_create(int device, cwlb_ctx** ctx);
+int cwlb_ctx_destroy(cwlb_ctx* ctx);
+/* Use an existing cudaStream_t (passed as void*) instead of the own stream. */
+int cwlb_ctx_set_stream(cwlb_ctx* ctx, void* cuda_stream);
+void* cwlb_ctx_stream(cwlb_ctx* ctx);
+/* Replaces q.wait(). */
+int cwlb_ctx_synchronize(cwlb_ctx* ctx);
+/* Device-side error flags raised by kernels since the last call (bit mask of
+ * CWLB_DEVERR_*); reading clears them.  Kernels never fault on bad indices:
+ * they skip the offending entry and raise a flag instead. */
+int cwlb_ctx_take_device_errors(cwlb_ctx* ctx, uint32_t* flags);
+#define CWLB_DEVERR_COL_RANGE 1u    /* a column index outside [0, h_rows) */
+#define CWLB_DEVERR_ROW_RANGE 2u    /* a task row outside [0, n_rows) */
+#define CWLB_DEVERR_OFFSETS 4u      /* row offsets not monotone or beyond nnz */
+#define CWLB_DEVERR_ORIGIN_RANGE 8u /* an origin id outside [0, n_rows) */
+/* Device queries the reference reads from sycl::device::get_info:
+ * max_work_group_size (parallelMatrix.cpp:76-77, main.cpp:359-361; 1024 on
+ * CUDA), max_compute_units (main.cpp:535-536, 718-719; the SM count),
+ * local_mem_size (parallelMatrix.cpp:349-350) and the device name. */
+int cwlb_device_info(cwlb_ctx* ctx, int64_t* max_work_group_size, int32_t* compute_units,
+                     int64_t* local_mem_size, char* name, size_t name_capacity);
+
+/* ------------------------------------------------------------------- SpMM */
+
+/* spmmKernel (include/parallelMatrix.h:13-20, src/parallelMatrix.cpp:63-254).
+ * Host buffers.  Inputs: the reordered CSR (row_offset[n_rows+1], col_ind and
+ * value[nnz], origin_local[n_rows]), H (h_rows x K, row-major) and the task
+ * list.  Writes out (n_rows x K, row-major, ORIGINAL row order; rows no task
+ * covers are zero) and *time_us (device time of the aggregation kernels, in
+ * microseconds, excluding transfers as the reference's event time does).
+ * dim_hint is unused and local_dimension is accepted for signature parity
+ * (the reference uses it only to size its local-memory staging tile).
+ * Errors: K > 1024 -> CWLB_ERR_INVALID_ARGUMENT (use the large-K entry);
+ * K == 0 or no tasks -> zero output and *time_us = 0, as the reference. */
+int cwlb_spmm_kernel(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* row_offset,
+                     const int32_t* col_ind, const float* value, const int32_t* origin_local,
+                     const float* H, int64_t h_rows, int64_t K, int32_t dim_hint,
+                     int32_t local_dimension, const cwlb_task* tasks, int64_t n_tasks,
+                     float* out, double* time_us);
+
+/* spmmKernelLargeKFallback (include/parallelMatrix.h:25-32,
+ * src/parallelMatrix.cpp:264-683): same contract; requires K > 1024
+ * (otherwise CWLB_ERR_INVALID_ARGUMENT, as the reference). */
+int cwlb_spmm_kernel_large_k(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
+                             const int32_t* row_offset, const int32_t* col_ind,
+                             const float* value, const int32_t* origin_local, const float* H,
+                             int64_t h_rows, int64_t K, int32_t dim_hint,
+                             int32_t local_dimension, const cwlb_task* tasks, int64_t n_tasks,
+                             float* out, double* time_us);
+
+/* Device-resident form of both entry points (any K >= 0), asynchronous on the
+ * context's stream, so that the CSR, H and tasks stay resident across
+ * launches (the reference's 70-launch timing loop, main.cpp:372-406).
+ * flags: 0 -> out is zero-filled first (reference semantics);
+ * CWLB_ROWS_COVERED -> the caller asserts that the tasks cover every row
+ * (see cwlb_tasks_check); the kernels then write every output row themselves
+ * and the full zero-fill is skipped. */
+#define CWLB_ROWS_COVERED 1u
+int cwlb_spmm_mean_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
+                          const int32_t* d_row_offset, const int32_t* d_col_ind,
+                          const float* d_value, const int32_t* d_origin_local, const float* d_H,
+                          int64_t h_rows, int64_t K, const cwlb_task* d_tasks, int64_t n_tasks,
+                          float* d_out, uint32_t flags);
+
+/* Validates a device task list against a reordered CSR (no counterpart in the
+ * reference, which trusts its partitioner): *bad_tasks counts tasks whose rows
+ * fall outside [0, n_rows); *uncovered_rows counts rows in no task's row
+ * range; *nnz_coverage_errors counts nonzeros not covered exactly once.
+ * Synchronous. */
+int cwlb_tasks_check(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* d_row_offset,
+                     const cwlb_task* d_tasks, int64_t n_tasks, int64_t* bad_tasks,
+                     int64_t* uncovered_rows, int64_t* nnz_coverage_errors);
+
+/* ---------------------------------------------------------- degree reorder */
+
+/* sortCSRByDegreeDPLCPU (main.cpp:197-278) on the GPU: rows ordered by
+ * (degree ascending, original id ascending), new offsets = inclusive scan of
+ * the sorted degrees, rows copied unchanged.  Bit-identical to the reference.
+ * Host buffers: origin_local[n_rows], sorted_row_offset[n_rows+1],
+ * sorted_col_ind[nnz], sorted_value[nnz].  n_rows == 0 returns an empty
+ * result.  Errors: CWLB_ERR_RUNTIME when row_offset[n_rows] != nnz. */
+int cwlb_sort_by_degree(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* row_offset,
+                        const int32_t* col_ind, const float* value, int32_t* origin_local,
+                        int32_t* sorted_row_offset, int32_t* sorted_col_ind,
+                        float* sorted_value);
+/* Device-buffer form (asynchronous). */
+int cwlb_sort_by_degree_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
+                               const int32_t* d_row_offset, const int32_t* d_col_ind,
+                               const float* d_value, int32_t* d_origin_local,
+                               int32_t* d_sorted_row_offset, int32_t* d_sorted_col_ind,
+                               float* d_sorted_value);
+
+/* ------------------------------------------------------------- partitioner */
+
+/* costWeightedTaskPartitioning (include/utils.h:57-60,
+ * src/utils.cpp:832-1021) on the GPU, bit-identical task list.
+ * row_offset: the reordered CSR's offsets (host, n_rows+1).  tasks may be
+ * NULL to query the count; if max_tasks is smaller than the count the call
+ * returns CWLB_ERR_BUFFER_TOO_SMALL with *n_tasks set. */
+int cwlb_partition(cwlb_ctx* ctx, int32_t n_rows, const int32_t* row_offset,
+                   const cwlb_costs* costs, double capacity, cwlb_task* tasks,
+                   int64_t max_tasks, int64_t* n_tasks);
+/* Device form: reads d_row_offset, writes the task list into context-owned
+ * device memory returned in *d_tasks (valid until the next partition call on
+ * this context) and its length in *n_tasks.  Synchronises once to learn the
+ * task count. */
+int cwlb_partition_device(cwlb_ctx* ctx, int32_t n_rows, const int32_t* d_row_offset,
+                          const cwlb_costs* costs, double capacity, cwlb_task** d_tasks,
+                          int64_t* n_tasks);
+
+/* ----------------------------------------------------- S-selection helpers */
+
+/* capacity_from_s (main.cpp:281-292). */
+double cwlb_capacity_from_s(int32_t s, const cwlb_costs* costs);
+/* The segment size S the partitioner derives from a capacity
+ * (src/utils.cpp:859-864). */
+int32_t cwlb_segment_size(const cwlb_costs* costs, double capacity);
+/* wave_based_s (main.cpp:295-321); CWLB_ERR_INVALID_ARGUMENT for
+ * compute_units <= 0 or wave <= 0. */
+int cwlb_wave_based_s(int64_t nnz, int32_t compute_units, int32_t wave, int32_t* s);
+/* recommended_candidate_w (main.cpp:87-95). */
+void cwlb_recommended_candidate_w(uint64_t nnz, int32_t out[3]);
+
+/* ------------------------------------------------------------- cost files */
+
+/* save_costs_one_per_line (src/utils.cpp:1024-1075): four lines, fixed
+ * notation with `precision` digits, order compute, load, store, atomic;
+ * creates the parent directory.  Returns CWLB_ERR_RUNTIME on failure. */
+int cwlb_save_costs(const cwlb_costs* costs, const char* path, int32_t append,
+                    int32_t precision);
+/* read_costs_one_per_line (src/utils.cpp:1077-1092). */
+int cwlb_read_costs(cwlb_costs* costs, const char* path);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CWLB_SPMM_H_ */

@@ -1,0 +1,85 @@
+"""GPU: the device-resident pipeline (sort -> partition -> aggregate) that the
+benchmark times, driven through the C ABI with torch-allocated buffers."""
+import numpy as np
+import pytest
+
+import cwlb_spmm as cs
+import graphs
+from helpers import assert_mean_close
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = cs.Context(0)
+    c.set_stream(torch.cuda.current_stream().cuda_stream)
+    yield c
+    c.close()
+
+
+def _device_pipeline(ctx, rowoff, col, val, X, costs, S):
+    dev = torch.device("cuda:0")
+    n, nnz = len(rowoff) - 1, len(col)
+    d_ro = torch.from_numpy(rowoff).to(dev)
+    d_col = torch.from_numpy(col).to(dev)
+    d_val = torch.from_numpy(val).to(dev)
+    d_X = torch.from_numpy(X).to(dev)
+    org = torch.empty(n, dtype=torch.int32, device=dev)
+    sro = torch.empty(n + 1, dtype=torch.int32, device=dev)
+    scol = torch.empty(max(nnz, 1), dtype=torch.int32, device=dev)
+    sval = torch.empty(max(nnz, 1), dtype=torch.float32, device=dev)
+    ctx.sort_by_degree_device(n, nnz, d_ro.data_ptr(), d_col.data_ptr(), d_val.data_ptr(),
+                              org.data_ptr(), sro.data_ptr(), scol.data_ptr(), sval.data_ptr())
+    cap = cs.capacity_from_s(S, costs)
+    t_ptr, n_tasks = ctx.partition_device(n, sro.data_ptr(), costs, cap)
+    return dict(org=org, sro=sro, scol=scol, sval=sval, X=d_X, t_ptr=t_ptr, n_tasks=n_tasks,
+                cap=cap, n=n, nnz=nnz)
+
+
+def test_device_pipeline_matches_oracle(ctx, oracle):
+    rowoff, col, val = graphs.rmat_np(14, 400_000, 0.57, 0.19, 0.19, seed=9, symmetrize=True,
+                                      drop_self_loops=True, dedupe=True)
+    n = len(rowoff) - 1
+    K = 64
+    X = graphs.uniform_features_np(n, K, seed=9)
+    costs = cs.SpmmCostParams(0.02, 0.7, 0.3, 0.5)
+    p = _device_pipeline(ctx, rowoff, col, val, X, costs, 24)
+    o = oracle.sort_by_degree(rowoff, col, val)
+    assert np.array_equal(p["org"].cpu().numpy(), o[0])
+    assert np.array_equal(p["sro"].cpu().numpy(), o[1])
+    assert np.array_equal(p["scol"][:p["nnz"]].cpu().numpy(), o[2])
+    want = oracle.partition(o[1], [0.02, 0.7, 0.3, 0.5], p["cap"])
+    torch.cuda.synchronize()
+    chk = ctx.tasks_check(n, p["nnz"], p["sro"].data_ptr(), p["t_ptr"], p["n_tasks"])
+    assert chk == dict(bad_tasks=0, uncovered_rows=0, nnz_coverage_errors=0)
+    out_full = torch.empty((n, K), dtype=torch.float32, device="cuda:0")
+    out_cov = torch.full((n, K), float("nan"), dtype=torch.float32, device="cuda:0")
+    args = (n, p["nnz"], p["sro"].data_ptr(), p["scol"].data_ptr(), p["sval"].data_ptr(),
+            p["org"].data_ptr(), p["X"].data_ptr(), n, K, p["t_ptr"], p["n_tasks"])
+    ctx.spmm_mean_device(*args, out_full.data_ptr(), 0)
+    ctx.spmm_mean_device(*args, out_cov.data_ptr(), cs.ROWS_COVERED)
+    torch.cuda.synchronize()
+    assert ctx.take_device_errors() == 0
+    ref, cond = oracle.spmm_mean_f64(o[1], o[2], o[3], o[0], X)
+    assert_mean_close(out_full.cpu().numpy(), ref, cond, what="device pipeline")
+    assert_mean_close(out_cov.cpu().numpy(), ref, cond, what="rows-covered mode")
+    # the task list itself, copied back through a host-buffer partition call
+    host_tasks = ctx.costWeightedTaskPartitioning(cs.CSR(o[1], o[2], o[3]), costs, p["cap"])
+    assert np.array_equal(host_tasks, want)
+    assert len(want) == p["n_tasks"]
+
+
+def test_tasks_check_detects_gaps(ctx):
+    rowoff = np.array([0, 2, 4, 4, 7], np.int32)
+    d_ro = torch.from_numpy(rowoff).cuda()
+    good = torch.tensor([[0, 2, 0, 0], [2, 4, 0, 0]], dtype=torch.int32, device="cuda:0")
+    gap = torch.tensor([[0, 1, 0, 0], [3, 4, 1, 0]], dtype=torch.int32, device="cuda:0")
+    bad = torch.tensor([[0, 9, 0, 0]], dtype=torch.int32, device="cuda:0")
+    assert ctx.tasks_check(4, 7, d_ro.data_ptr(), good.data_ptr(), 2) == dict(
+        bad_tasks=0, uncovered_rows=0, nnz_coverage_errors=0)
+    r = ctx.tasks_check(4, 7, d_ro.data_ptr(), gap.data_ptr(), 2)
+    assert r["uncovered_rows"] == 2 and r["nnz_coverage_errors"] == 3
+    assert ctx.tasks_check(4, 7, d_ro.data_ptr(), bad.data_ptr(), 1)["bad_tasks"] == 1

@@ -1,0 +1,243 @@
+"""GPU parity: the sm_100a path through the C ABI against the oracle.
+
+Bit-exact: the degree permutation, reordered CSR and task list.
+Within REL_TOL (tests/helpers.py): the mean-aggregation output.
+"""
+import numpy as np
+import pytest
+
+import cwlb_spmm as cs
+import graphs
+from conftest import load_npz
+from helpers import REL_TOL, assert_mean_close, random_csr, sorted_rowoff_from_degrees
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = cs.Context(0)
+    yield c
+    c.close()
+
+
+def test_device_info(ctx):
+    info = ctx.device_info()
+    assert info["max_work_group_size"] == 1024
+    assert info["max_compute_units"] >= 100
+    assert info["local_mem_size"] > 0
+
+
+def _oracle_pipeline(oracle, rowoff, col, val, costs, S):
+    origin, srow, scol, sval = oracle.sort_by_degree(rowoff, col, val)
+    cap = oracle.capacity_from_s(S, costs)
+    tasks = oracle.partition(srow, costs, cap)
+    return origin, srow, scol, sval, cap, tasks
+
+
+def test_cfg1_golden_end_to_end(ctx, oracle):
+    g = load_npz("cfg1_er4096.npz")
+    rowoff, col = g["rowoff"], g["col"]
+    val = np.ones(len(col), np.float32)
+    X = graphs.uniform_features_np(4096, 32, seed=0)
+    order = ctx.sortCSRByDegree(cs.CSR(rowoff, col, val))
+    assert np.array_equal(order.Origin_local, g["origin"])
+    assert np.array_equal(order.RowOffset, g["sorted_rowoff"])
+    o = oracle.sort_by_degree(rowoff, col, val)
+    assert np.array_equal(order.ColInd, o[2]) and np.array_equal(order.Value, o[3])
+    costs = cs.SpmmCostParams.from_list(g["costs"])
+    cap = cs.capacity_from_s(32, costs)
+    assert cap == float(g["capacity"])
+    tasks = ctx.costWeightedTaskPartitioning(order, costs, cap)
+    assert np.array_equal(tasks, g["tasks"])
+    out, t_us = ctx.spmmKernel(order, X, 32, 32, tasks)
+    assert t_us > 0
+    ref, cond = oracle.spmm_mean_f64(order.RowOffset, order.ColInd, order.Value,
+                                     order.Origin_local, X)
+    assert_mean_close(out, ref, cond, what="cfg1 vs f64")
+    assert_mean_close(out, g["out"].astype(np.float64), cond, tol=2 * REL_TOL, what="cfg1 vs ref")
+    assert np.abs(out - g["out"]).max() <= 1e-4  # the reference's own check (utils.h:83)
+
+
+def test_partition_golden_cases_bit_exact(ctx):
+    g = load_npz("partition_cases.npz")
+    rp, tp = g["rowoff_ptr"], g["task_ptr"]
+    for i in range(len(g["S"])):
+        ro = g["rowoff"][rp[i]:rp[i + 1]]
+        want = g["tasks"][tp[i]:tp[i + 1]]
+        csr = cs.CSR(ro, np.zeros(ro[-1], np.int32), np.zeros(ro[-1], np.float32))
+        costs = cs.SpmmCostParams.from_list(g["cost_sets"][g["cset"][i]])
+        got = ctx.costWeightedTaskPartitioning(csr, costs, g["capacity"][i])
+        assert np.array_equal(got, want), f"partition golden case {i}"
+
+
+def _partition_case(rng, it):
+    n = int(rng.integers(1, 600))
+    kind = it % 6
+    if kind == 0:
+        d = rng.integers(0, 30, n)
+    elif kind == 1:
+        d = np.minimum((rng.pareto(1.2, n) * 4).astype(int), 3000)
+    elif kind == 2:
+        d = np.repeat(rng.integers(0, 90, 6), n // 6 + 1)[:n]
+    elif kind == 3:
+        d = rng.integers(0, 4, n) * rng.integers(0, 50, n)
+    elif kind == 4:
+        d = np.full(n, int(rng.integers(0, 400)))
+    else:
+        d = rng.integers(0, 3, n)
+    costs = cs.SpmmCostParams(rng.uniform(0.01, 2), rng.uniform(0.01, 2),
+                              float(rng.choice([0.0, rng.uniform(-1, 3)])), rng.uniform(0, 6))
+    S = int(rng.choice([1, 2, 3, 5, 8, 16, 31, 64, 200, 5000]))
+    cap = cs.capacity_from_s(S, costs)
+    if it % 7 == 0:
+        cap *= rng.uniform(0.1, 3)
+    return sorted_rowoff_from_degrees(d), costs, cap
+
+
+def test_partition_random_vs_oracle(ctx, oracle):
+    rng = np.random.default_rng(11)
+    for it in range(400):
+        ro, costs, cap = _partition_case(rng, it)
+        want = oracle.partition(ro, [costs.C_compute_ns, costs.C_load_ns, costs.C_store_ns,
+                                     costs.C_atomic_ns], cap)
+        csr = cs.CSR(ro, np.zeros(ro[-1], np.int32), np.zeros(ro[-1], np.float32))
+        got = ctx.costWeightedTaskPartitioning(csr, costs, cap)
+        assert np.array_equal(got, want), f"random partition case {it}"
+
+
+@pytest.mark.parametrize("costs,cap", [
+    ((float("nan"), 1.0, 0.5, 2.0), 40.0),       # non-finite costs: literal path
+    ((0.0, 0.0, 0.5, 2.0), 10.0),                # Cc + Cl == 0
+    ((-0.5, 0.2, 0.5, 2.0), 10.0),               # Cc + Cl < 0
+    ((0.3, 0.4, 0.5, 1.0), float("inf")),        # infinite capacity
+    ((0.3, 0.4, 0.5, 1.0), float("nan")),        # NaN capacity
+    ((0.3, 0.4, 1e9, 1.0), 50.0),                # every row long, empty rows dropped
+    ((0.3, 0.4, 0.0, 1.0), 5.0),                 # zero-weight empty rows
+    ((0.3, 0.4, -2.0, 1.0), 5.0),                # negative store cost
+])
+def test_partition_edge_costs_vs_oracle(ctx, oracle, costs, cap):
+    rng = np.random.default_rng(5)
+    d = np.concatenate([np.zeros(50, int), rng.integers(1, 40, 300), [500, 2000]])
+    ro = sorted_rowoff_from_degrees(d)
+    want = oracle.partition(ro, list(costs), cap)
+    csr = cs.CSR(ro, np.zeros(ro[-1], np.int32), np.zeros(ro[-1], np.float32))
+    got = ctx.costWeightedTaskPartitioning(csr, cs.SpmmCostParams.from_list(costs), cap)
+    assert np.array_equal(got, want)
+
+
+def test_partition_unsorted_rows_vs_oracle(ctx, oracle):
+    rng = np.random.default_rng(6)
+    for _ in range(30):
+        d = rng.integers(0, 120, int(rng.integers(2, 300)))  # not degree-sorted
+        ro = np.zeros(len(d) + 1, np.int32)
+        ro[1:] = np.cumsum(d)
+        costs = [0.2, 0.5, 0.3, 1.0]
+        cap = oracle.capacity_from_s(16, costs)
+        csr = cs.CSR(ro, np.zeros(ro[-1], np.int32), np.zeros(ro[-1], np.float32))
+        got = ctx.costWeightedTaskPartitioning(csr, cs.SpmmCostParams.from_list(costs), cap)
+        assert np.array_equal(got, oracle.partition(ro, costs, cap))
+
+
+@pytest.mark.parametrize("n,maxdeg,hub", [(1, 5, 1), (7, 0, 1), (300, 40, 3), (5000, 20, 70000),
+                                          (20000, 300, 50), (70000, 3, 1)])
+def test_sort_vs_oracle(ctx, oracle, n, maxdeg, hub):
+    rng = np.random.default_rng(n + maxdeg)
+    rowoff, col, val = random_csr(rng, n, maxdeg, hubs=1, hub_factor=hub)
+    got = ctx.sortCSRByDegree(cs.CSR(rowoff, col, val))
+    want = oracle.sort_by_degree(rowoff, col, val)
+    assert np.array_equal(got.Origin_local, want[0])
+    assert np.array_equal(got.RowOffset, want[1])
+    assert np.array_equal(got.ColInd, want[2])
+    assert np.array_equal(got.Value, want[3])
+
+
+def test_sort_rejects_inconsistent_nnz(ctx):
+    with pytest.raises(RuntimeError, match="inconsistent NNZ"):
+        ctx.sortCSRByDegree(cs.CSR(np.array([0, 2, 5], np.int32), np.zeros(4, np.int32),
+                                   np.zeros(4, np.float32)))
+
+
+def test_spmm_golden_cases(ctx, oracle):
+    g = load_npz("spmm_cases.npz")
+    for c in range(int(g["n_cases"])):
+        f = {k: g[f"c{c}_{k}"] for k in ("rowoff", "col", "val", "origin", "H", "tasks", "out")}
+        K = int(g[f"c{c}_K"])
+        order = cs.CSR_Order(f["rowoff"], f["col"], f["val"], f["origin"])
+        fn = ctx.spmmKernelLargeKFallback if K > 1024 else ctx.spmmKernel
+        out, _ = fn(order, f["H"], K, K, f["tasks"])
+        ref, cond = oracle.spmm_mean_f64(f["rowoff"], f["col"], f["val"], f["origin"], f["H"])
+        assert_mean_close(out, ref, cond, what=f"golden spmm case {c} K={K}")
+        assert_mean_close(out, f["out"].astype(np.float64), cond, tol=2 * REL_TOL,
+                          what=f"golden spmm case {c} K={K} vs reference")
+
+
+KS = [1, 2, 3, 4, 5, 8, 12, 16, 24, 31, 32, 33, 48, 64, 96, 100, 128, 160, 256, 384, 512, 640,
+      1000, 1024]
+
+
+@pytest.mark.parametrize("K", KS)
+def test_spmm_random_vs_oracle(ctx, oracle, K):
+    rng = np.random.default_rng(K)
+    n = 700
+    rowoff, col, val = random_csr(rng, n, 60, hubs=2, hub_factor=40)
+    H = rng.uniform(-1, 1, (n, K)).astype(np.float32)
+    for S in (1, 7, 32, 300):
+        costs = [0.1, 0.6, 0.4, 0.9]
+        origin, srow, scol, sval, cap, tasks = _oracle_pipeline(oracle, rowoff, col, val, costs, S)
+        order = cs.CSR_Order(srow, scol, sval, origin)
+        out, _ = ctx.spmmKernel(order, H, K, K, tasks)
+        ref, cond = oracle.spmm_mean_f64(srow, scol, sval, origin, H)
+        assert_mean_close(out, ref, cond, what=f"K={K} S={S}")
+        o32 = oracle.spmm_mean(srow, scol, sval, origin, H, tasks)
+        assert np.abs(out - o32).max() <= 1e-4
+
+
+@pytest.mark.parametrize("K", [1025, 1100, 1536, 2048, 3001])
+def test_spmm_large_k_vs_oracle(ctx, oracle, K):
+    rng = np.random.default_rng(K)
+    n = 120
+    rowoff, col, val = random_csr(rng, n, 50, hubs=1, hub_factor=10)
+    H = rng.standard_normal((n, K)).astype(np.float32)
+    origin, srow, scol, sval, cap, tasks = _oracle_pipeline(oracle, rowoff, col, val,
+                                                            [0.1, 0.6, 0.4, 0.9], 16)
+    order = cs.CSR_Order(srow, scol, sval, origin)
+    out, _ = ctx.spmmKernelLargeKFallback(order, H, K, K, tasks)
+    ref, cond = oracle.spmm_mean_f64(srow, scol, sval, origin, H)
+    assert_mean_close(out, ref, cond, what=f"large K={K}")
+
+
+def test_spmm_error_behaviour(ctx):
+    order = cs.CSR_Order(np.array([0, 1], np.int32), np.array([0], np.int32),
+                         np.ones(1, np.float32), np.zeros(1, np.int32))
+    tasks = np.array([[0, 1, 0, 0]], np.int32)
+    with pytest.raises(ValueError, match="K <= device max work-group size"):
+        ctx.spmmKernel(order, np.ones((1, 1025), np.float32), 0, 1025, tasks)
+    with pytest.raises(ValueError, match="requires K > device max work-group size"):
+        ctx.spmmKernelLargeKFallback(order, np.ones((1, 64), np.float32), 0, 64, tasks)
+    out, t = ctx.spmmKernel(order, np.ones((1, 0), np.float32), 0, 0, tasks)
+    assert out.shape == (1, 0) and t == 0.0
+    out, t = ctx.spmmKernel(order, np.full((1, 8), 3.0, np.float32), 8, 8,
+                            np.zeros((0, 4), np.int32))
+    assert not out.any() and t == 0.0
+    with pytest.raises(ValueError):
+        ctx.spmmKernel(order, np.ones((1, 8), np.float32), 8, 0, tasks)
+
+
+def test_spmm_bad_indices_raise_without_fault(ctx):
+    H = np.ones((4, 16), np.float32)
+    good = cs.CSR_Order(np.array([0, 2, 3, 3, 4], np.int32), np.array([0, 1, 2, 3], np.int32),
+                        np.ones(4, np.float32), np.array([3, 2, 1, 0], np.int32))
+    tasks = np.array([[0, 4, 0, 0]], np.int32)
+    bad_col = cs.CSR_Order(good.RowOffset, np.array([0, 9, 2, -1], np.int32), good.Value,
+                           good.Origin_local)
+    with pytest.raises(ValueError, match="column index"):
+        ctx.spmmKernel(bad_col, H, 16, 16, tasks)
+    with pytest.raises(ValueError, match="task row"):
+        ctx.spmmKernel(good, H, 16, 16, np.array([[0, 9, 0, 0]], np.int32))
+    bad_origin = cs.CSR_Order(good.RowOffset, good.ColInd, good.Value,
+                              np.array([3, 2, 7, 0], np.int32))
+    with pytest.raises(ValueError, match="Origin_local"):
+        ctx.spmmKernel(bad_origin, H, 16, 16, tasks)
+    out, _ = ctx.spmmKernel(good, H, 16, 16, tasks)  # the context still works
+    assert np.allclose(out[[3, 2, 0]], 1.0) and not out[1].any()
