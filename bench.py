@@ -58,6 +58,10 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target CPU time of the CPU-baseline sample")
+    ap.add_argument("--scale-down", type=int, default=1,
+                    help="shrink the configuration (profiling captures only; not a bench line)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     return ap.parse_args()
 
 
@@ -197,9 +201,9 @@ def shard_bounds(rowoff_t, costs, world, rank):
     return min(cut(rank), n), min(cut(rank + 1), n)
 
 
-def build_workload(cfg_id, device, world, rank, costs):
+def build_workload(cfg_id, device, world, rank, costs, scale_down=1):
     import torch
-    rowoff, col, val, X = graphs.build_config_torch(cfg_id, device)
+    rowoff, col, val, X = graphs.build_config_torch(cfg_id, device, scale_down=scale_down)
     a, b = shard_bounds(rowoff, costs, world, rank)
     e0, e1 = int(rowoff[a]), int(rowoff[b])
     ro = (rowoff[a:b + 1] - e0).contiguous()
@@ -333,7 +337,7 @@ def run_ours(args):
     torch.cuda.set_device(device)
     costs = read_costs()
     cfg = graphs.CONFIGS[args.config]
-    wl = build_workload(args.config, device, world, rank, costs)
+    wl = build_workload(args.config, device, world, rank, costs, args.scale_down)
     ctx = cs.Context(local)
     ctx.set_stream(torch.cuda.current_stream().cuda_stream)
     device_prepare(ctx, wl)
@@ -389,29 +393,34 @@ def run_ours(args):
     peak, peak_kind = hbm_peak()
     achieved = bytes_local / per_launch / 1e9
 
-    # e2e: host buffers through the reference-facing call (spmmKernel)
-    sro = wl["sro"].cpu().pin_memory()
-    scol = wl["scol"][:wl["nnz"]].cpu().pin_memory()
-    sval = wl["sval"][:wl["nnz"]].cpu().pin_memory()
-    org = wl["org"][:wl["n"]].cpu().pin_memory()
-    Xh = wl["X"].cpu().pin_memory()
-    th = tasks[:n_tasks].cpu().pin_memory()
-    outh = torch.empty((wl["n"], K), dtype=torch.float32).pin_memory()
-    order = cs.CSR_Order(sro.numpy(), scol.numpy(), sval.numpy(), org.numpy())
-    call = ctx.spmmKernel if K <= 1024 else ctx.spmmKernelLargeKFallback
-    call(order, Xh.numpy(), K, K, th.numpy(), out=outh.numpy())  # warm
-    e2e_steps = max(1, min(args.e2e_steps, args.steps))
-    barrier(world)
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        call(order, Xh.numpy(), K, K, th.numpy(), out=outh.numpy())
-    t_e2e = allreduce_max(time.perf_counter() - t0, world)
-    h2d = (sro.numel() + scol.numel() + sval.numel() + org.numel() + Xh.numel() +
-           th.numel()) * 4
-    d2h = outh.numel() * 4
+    e2e = None
+    if not args.no_e2e:
+        # e2e: host buffers through the reference-facing call (spmmKernel)
+        sro = wl["sro"].cpu().pin_memory()
+        scol = wl["scol"][:wl["nnz"]].cpu().pin_memory()
+        sval = wl["sval"][:wl["nnz"]].cpu().pin_memory()
+        org = wl["org"][:wl["n"]].cpu().pin_memory()
+        Xh = wl["X"].cpu().pin_memory()
+        th = tasks[:n_tasks].cpu().pin_memory()
+        outh = torch.empty((wl["n"], K), dtype=torch.float32).pin_memory()
+        order = cs.CSR_Order(sro.numpy(), scol.numpy(), sval.numpy(), org.numpy())
+        call = ctx.spmmKernel if K <= 1024 else ctx.spmmKernelLargeKFallback
+        call(order, Xh.numpy(), K, K, th.numpy(), out=outh.numpy())  # warm
+        e2e_steps = max(1, min(args.e2e_steps, args.steps))
+        barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            call(order, Xh.numpy(), K, K, th.numpy(), out=outh.numpy())
+        t_e2e = allreduce_max(time.perf_counter() - t0, world)
+        h2d = (sro.numel() + scol.numel() + sval.numel() + org.numel() + Xh.numel() +
+               th.numel()) * 4
+        d2h = outh.numel() * 4
+        e2e = {"value": round(flops_total / (t_e2e / e2e_steps) / 1e9, 2), "unit": "GFLOP/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": round(t_e2e / e2e_steps * 1e3, 3)}
 
     cpu = None
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(wl, tasks[:n_tasks].cpu().numpy(), args.cpu_seconds)
 
     if rank == 0:
@@ -422,7 +431,8 @@ def run_ours(args):
             "ms_per_step": round(t_max / args.steps * 1e3, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded generator, unit edge values)",
-            "config": {"workload": f"config {args.config}: {cfg['name']}",
+            "config": {"workload": f"config {args.config}: {cfg['name']}" +
+                       (f" scaled down {args.scale_down}x" if args.scale_down > 1 else ""),
                        "rows": wl["n_total"], "nnz": wl["nnz_total"], "K": K, "S": S,
                        "n_tasks_rank0": n_tasks, "costs": os.path.relpath(COSTS_FILE, ROOT),
                        "parallelism": f"row shards x{world}" if world > 1 else "single GPU",
@@ -433,9 +443,7 @@ def run_ours(args):
                          "peak_source": peak_kind, "traffic": None,
                          "algorithmic_bytes_per_launch": bytes_local,
                          "launch_us": round(per_launch * 1e6, 2)},
-            "e2e": {"value": round(flops_total / (t_e2e / e2e_steps) / 1e9, 2), "unit": "GFLOP/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": round(t_e2e / e2e_steps * 1e3, 3)},
+            "e2e": e2e,
             "gpu_launches": (2 if flags else 1) * args.steps,
             "clocks": clocks,
         }
@@ -490,7 +498,8 @@ def run_reference(args):
             "value": round(v, 3), "unit": "GFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator)",
-            "config": {"workload": f"config {args.config}: {cfg['name']}", "rows": len(origin),
+            "config": {"workload": f"config {args.config}: {cfg['name']}" +
+                       (f" scaled down {args.scale_down}x" if args.scale_down > 1 else ""), "rows": len(origin),
                        "nnz": nnz, "K": K, "S": S},
             "cpu_baseline": {"value": round(v, 3), "unit": "GFLOP/s",
                              "cores": samples[-1]["cores"], "kind": "port",

@@ -109,11 +109,11 @@ __device__ __forceinline__ int row_fragment(const SpmmArgs& a, int r, const cwlb
 }
 
 __device__ __forceinline__ bool load_task(const SpmmArgs& a, int64_t t, cwlb_task& tk) {
-    const int4 raw = __ldg(reinterpret_cast<const int4*>(a.tasks) + t);
-    tk.row_start = raw.x;
-    tk.row_end = raw.y;
-    tk.first_row_offset = raw.z;
-    tk.last_row_nnz = raw.w;
+    // Scalar loads: a caller's task array need only be 4-byte aligned.
+    tk.row_start = __ldg(&a.tasks[t].row_start);
+    tk.row_end = __ldg(&a.tasks[t].row_end);
+    tk.first_row_offset = __ldg(&a.tasks[t].first_row_offset);
+    tk.last_row_nnz = __ldg(&a.tasks[t].last_row_nnz);
     if (tk.row_start < 0 || tk.row_end > a.n_rows || tk.row_start > tk.row_end) {
         raise_err(a.err, CWLB_DEVERR_ROW_RANGE);
         return false;
@@ -353,8 +353,8 @@ __global__ void __launch_bounds__(kThreads) zero_split_rows_kernel(SpmmArgs a) {
     const int lane = threadIdx.x & 31;
     const int64_t t = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
     if (t >= a.n_tasks) return;
-    const int4 raw = __ldg(reinterpret_cast<const int4*>(a.tasks) + t);
-    cwlb_task tk{raw.x, raw.y, raw.z, raw.w};
+    const cwlb_task tk{__ldg(&a.tasks[t].row_start), __ldg(&a.tasks[t].row_end),
+                       __ldg(&a.tasks[t].first_row_offset), __ldg(&a.tasks[t].last_row_nnz)};
     if (tk.row_start < 0 || tk.row_end > a.n_rows || tk.row_start >= tk.row_end) return;
     const int rows[2] = {tk.row_start, tk.row_end - 1};
     const int n = rows[0] == rows[1] ? 1 : 2;
@@ -542,8 +542,11 @@ void run_tasks_check(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* 
                      const cwlb_task* tasks, int64_t n_tasks, int64_t* bad_tasks,
                      int64_t* uncovered_rows, int64_t* nnz_errors) {
     cudaStream_t s = ctx->stream;
-    const size_t rows_b = sizeof(uint32_t) * static_cast<size_t>(n_rows > 0 ? n_rows : 0);
-    const size_t nnz_b = sizeof(uint32_t) * static_cast<size_t>(nnz > 0 ? nnz : 0);
+    // Each piece starts on a 256-byte boundary (the 64-bit counters need
+    // 8-byte alignment for their atomics).
+    auto al = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
+    const size_t rows_b = al(sizeof(uint32_t) * static_cast<size_t>(n_rows > 0 ? n_rows : 0));
+    const size_t nnz_b = al(sizeof(uint32_t) * static_cast<size_t>(nnz > 0 ? nnz : 0));
     char* base = static_cast<char*>(ctx->check_scratch.ensure(rows_b + nnz_b + 64));
     uint32_t* row_seen = reinterpret_cast<uint32_t*>(base);
     uint32_t* nnz_count = reinterpret_cast<uint32_t*>(base + rows_b);

@@ -230,7 +230,7 @@ CONFIGS = {
             K=32, features=("uniform", 0), S=32),
     # R-MAT directed samples before self-loop removal, symmetrisation and
     # de-duplication; 6.2e7 samples leave ~1.1e8 stored nonzeros.
-    2: dict(name="rmat18_k128", graph=("rmat", dict(scale=18, n_edges=62_000_000, a=0.57,
+    2: dict(name="rmat18_k128", graph=("rmat", dict(scale=18, n_edges=85_000_000, a=0.57,
                                                      b=0.19, c=0.19, seed=1, symmetrize=True,
                                                      drop_self_loops=True, dedupe=True)),
             K=128, features=("uniform", 1), S=None),
