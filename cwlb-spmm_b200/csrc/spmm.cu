@@ -123,67 +123,94 @@ __device__ __forceinline__ bool load_task(const SpmmArgs& a, int64_t t, cwlb_tas
 
 // ---------------------------------------------------------------------------
 // float4 kernel: L lanes per group, V float4 per lane, U nonzeros per step.
+//
+// Index handling: a group walks its nonzeros in chunks of L.  Each lane loads
+// one (col, value) pair of the chunk with a coalesced load and validates it
+// (an out-of-range column becomes (0, 0.0f) and raises CWLB_DEVERR_COL_RANGE);
+// the pairs are then broadcast inside the group with __shfl_sync, so every
+// nonzero costs two shuffles, one wide address multiply-add, V 16-byte loads
+// and 4V FMAs.  Loads are unconditional: lanes past the end of a partial
+// chunk hold column 0 (valid) and skip only the FMA; padding lanes of a
+// partial K tile read a valid column and never write.
 
 template <int L, int V>
 struct VecCfg {
     static constexpr int G = 32 / L;
-    static constexpr int U = V == 1 ? 8 : (V == 2 ? 4 : 2);
+    static constexpr int U0 = V == 1 ? 8 : (V == 2 ? 4 : 2);
+    static constexpr int U = U0 < L ? U0 : L;
 };
 
-// Gather-accumulate nonzeros j = j0, j0 + step, ... < j1 into acc (per column
-// the FMA chain follows increasing j).
+// Accumulate the nonzeros of chunks starting at `start`, `start + step`, ...
+// (each at most L long, ending at `end`) into acc.  All lanes of the group
+// execute this with the same arguments.  Per column, the FMA chain follows
+// increasing nonzero index within each chunk and chunk order.
 template <int L, int V>
-__device__ __forceinline__ void gather_accumulate(const SpmmArgs& a, int32_t j0, int32_t j1,
-                                                  int32_t step, const int64_t (&q)[V],
-                                                  const bool (&ok)[V], float4 (&acc)[V]) {
+__device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, int32_t end,
+                                              int32_t step, unsigned gmask, int lg,
+                                              const float4* const (&hq)[V], const bool (&ok)[V],
+                                              uint32_t K4, float4 (&acc)[V]) {
     constexpr int U = VecCfg<L, V>::U;
-    const float4* __restrict__ H4 = reinterpret_cast<const float4*>(a.H);
-    const int64_t K4 = a.K >> 2;
-    int32_t j = j0;
-    for (; j + (U - 1) * step < j1; j += U * step) {
-        int32_t c[U];
-        float v[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            c[u] = __ldg(a.col + j + u * step);
-            v[u] = __ldg(a.val + j + u * step);
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (static_cast<uint64_t>(c[u]) >= static_cast<uint64_t>(a.h_rows)) {
+    for (int32_t pos = start; pos < end; pos += step) {
+        const int32_t cnt = min(L, end - pos);
+        int32_t c = 0;
+        float v = 0.0f;
+        if (lg < cnt) {
+            c = __ldg(a.col + pos + lg);
+            v = __ldg(a.val + pos + lg);
+            if (static_cast<uint32_t>(c) >= static_cast<uint64_t>(a.h_rows)) {
                 raise_err(a.err, CWLB_DEVERR_COL_RANGE);
-                c[u] = 0;
-                v[u] = 0.0f;
+                c = 0;
+                v = 0.0f;
             }
         }
-        float4 x[U][V];
+        if (cnt == L) {
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
+            for (int u0 = 0; u0 < L; u0 += U) {
+                uint32_t cu[U];
+                float vu[U];
 #pragma unroll
-            for (int i = 0; i < V; ++i) {
-                x[u][i] = ok[i] ? __ldg(H4 + static_cast<int64_t>(c[u]) * K4 + q[i])
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int t = 0; t < U; ++t) {
+                    cu[t] = static_cast<uint32_t>(__shfl_sync(gmask, c, u0 + t, L));
+                    vu[t] = __shfl_sync(gmask, v, u0 + t, L);
+                }
+                float4 x[U][V];
+#pragma unroll
+                for (int t = 0; t < U; ++t) {
+#pragma unroll
+                    for (int i = 0; i < V; ++i)
+                        x[t][i] = __ldg(hq[i] + static_cast<size_t>(cu[t]) * K4);
+                }
+#pragma unroll
+                for (int t = 0; t < U; ++t) {
+#pragma unroll
+                    for (int i = 0; i < V; ++i) acc[i] = fma4(vu[t], x[t][i], acc[i]);
+                }
             }
-        }
+        } else {
+            for (int32_t u0 = 0; u0 < cnt; u0 += U) {
+                uint32_t cu[U];
+                float vu[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
+                for (int t = 0; t < U; ++t) {
+                    const int src = (u0 + t) & (L - 1);
+                    cu[t] = static_cast<uint32_t>(__shfl_sync(gmask, c, src, L));
+                    vu[t] = __shfl_sync(gmask, v, src, L);
+                }
+                float4 x[U][V];
 #pragma unroll
-            for (int i = 0; i < V; ++i) acc[i] = fma4(v[u], x[u][i], acc[i]);
-        }
-    }
-    for (; j < j1; j += step) {
-        int32_t c = __ldg(a.col + j);
-        float v = __ldg(a.val + j);
-        if (static_cast<uint64_t>(c) >= static_cast<uint64_t>(a.h_rows)) {
-            raise_err(a.err, CWLB_DEVERR_COL_RANGE);
-            c = 0;
-            v = 0.0f;
-        }
+                for (int t = 0; t < U; ++t) {
 #pragma unroll
-        for (int i = 0; i < V; ++i) {
-            const float4 x = ok[i] ? __ldg(H4 + static_cast<int64_t>(c) * K4 + q[i])
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-            acc[i] = fma4(v, x, acc[i]);
+                    for (int i = 0; i < V; ++i)
+                        x[t][i] = __ldg(hq[i] + static_cast<size_t>(cu[t]) * K4);
+                }
+#pragma unroll
+                for (int t = 0; t < U; ++t) {
+                    if (u0 + t < cnt) {
+#pragma unroll
+                        for (int i = 0; i < V; ++i) acc[i] = fma4(vu[t], x[t][i], acc[i]);
+                    }
+                }
+            }
         }
     }
 }
@@ -207,6 +234,15 @@ __device__ __forceinline__ void write_row(const SpmmArgs& a, const RowFrag& f,
     }
 }
 
+template <int V>
+__device__ __forceinline__ void write_zero_row(const SpmmArgs& a, int32_t orig,
+                                               const int64_t (&q)[V], const bool (&ok)[V]) {
+    float4* out4 = reinterpret_cast<float4*>(a.out) + static_cast<int64_t>(orig) * (a.K >> 2);
+#pragma unroll
+    for (int i = 0; i < V; ++i)
+        if (ok[i]) __stcs(out4 + q[i], make_float4(0.f, 0.f, 0.f, 0.f));
+}
+
 template <int L, int V>
 __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
     constexpr int G = VecCfg<L, V>::G;
@@ -218,58 +254,54 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
 
     const int g = lane / L;
     const int lg = lane % L;
-    const int64_t K4 = a.K >> 2;
+    const unsigned gmask = L == 32 ? 0xffffffffu : (((1u << L) - 1u) << (g * L));
+    const uint32_t K4 = static_cast<uint32_t>(a.K >> 2);
     const int64_t q0 = static_cast<int64_t>(blockIdx.y) * (L * V);
+    const float4* __restrict__ H4 = reinterpret_cast<const float4*>(a.H);
     int64_t q[V];
     bool ok[V];
+    const float4* hq[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) {
         q[i] = q0 + lg + i * L;
-        ok[i] = q[i] < K4;
+        ok[i] = q[i] < static_cast<int64_t>(K4);
+        // Padding lanes read a valid column (the row's last) and never write.
+        hq[i] = H4 + (ok[i] ? q[i] : static_cast<int64_t>(K4) - 1);
     }
     const int n_task_rows = tk.row_end - tk.row_start;
 
     if (G == 1 || n_task_rows != 1) {
-        // Each group takes its own rows; nnz order within a row is preserved.
+        // Each group takes its own rows (nnz order within a row preserved).
         for (int r = tk.row_start + g; r < tk.row_end; r += G) {
             RowFrag f;
             const int st = row_fragment(a, r, tk, f);
             if (st == 1) {
-                if (a.write_empty) {
-                    float4* out4 = reinterpret_cast<float4*>(a.out) +
-                                   static_cast<int64_t>(f.orig) * K4;
-#pragma unroll
-                    for (int i = 0; i < V; ++i)
-                        if (ok[i]) __stcs(out4 + q[i], make_float4(0.f, 0.f, 0.f, 0.f));
-                }
+                if (a.write_empty) write_zero_row<V>(a, f.orig, q, ok);
                 continue;
             }
             if (st != 0) continue;
             float4 acc[V];
 #pragma unroll
             for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            gather_accumulate<L, V>(a, f.base + f.begin, f.base + f.end, 1, q, ok, acc);
+            gather_chunks<L, V>(a, f.base + f.begin, f.base + f.end, L, gmask, lg, hq, ok, K4,
+                                acc);
             write_row<V>(a, f, q, ok, acc);
         }
     } else {
-        // One row: the G groups split its nonzeros, then reduce by shuffles.
-        const int r = tk.row_start;
+        // One row: the G groups take interleaved chunks, then reduce by
+        // shuffles across groups.
         RowFrag f;
-        const int st = row_fragment(a, r, tk, f);
+        const int st = row_fragment(a, tk.row_start, tk, f);
         if (st == 1) {
-            if (a.write_empty && g == 0) {
-                float4* out4 = reinterpret_cast<float4*>(a.out) + static_cast<int64_t>(f.orig) * K4;
-#pragma unroll
-                for (int i = 0; i < V; ++i)
-                    if (ok[i]) __stcs(out4 + q[i], make_float4(0.f, 0.f, 0.f, 0.f));
-            }
+            if (a.write_empty && g == 0) write_zero_row<V>(a, f.orig, q, ok);
             return;
         }
         if (st != 0) return;
         float4 acc[V];
 #pragma unroll
         for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        gather_accumulate<L, V>(a, f.base + f.begin + g, f.base + f.end, G, q, ok, acc);
+        gather_chunks<L, V>(a, f.base + f.begin + g * L, f.base + f.end, 32, gmask, lg, hq, ok,
+                            K4, acc);
 #pragma unroll
         for (int s = L; s < 32; s <<= 1) {
 #pragma unroll
