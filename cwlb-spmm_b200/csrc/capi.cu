@@ -144,6 +144,8 @@ cwlb_costs zero_costs() {
 
 }  // namespace
 
+void cwlb::set_last_error(const std::string& msg) { g_last_error = msg; }
+
 extern "C" {
 
 const char* cwlb_last_error(void) { return g_last_error.c_str(); }

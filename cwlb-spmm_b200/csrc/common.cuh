@@ -88,5 +88,7 @@ void launch_sort_by_degree(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int
 // Returns the number of tasks; the tasks are in ctx->part_tasks.
 int64_t run_partition(cwlb_ctx* ctx, int32_t n_rows, const int32_t* d_rowoff,
                       const cwlb_costs& costs, double capacity);
+// Sets the calling thread's cwlb_last_error() message (defined in capi.cu).
+void set_last_error(const std::string& msg);
 
 }  // namespace cwlb

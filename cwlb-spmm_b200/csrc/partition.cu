@@ -41,6 +41,8 @@
 // single-thread restatement of the reference loop instead.  No loop here
 // waits on another thread; every loop is bounded by the input size.
 #include <cmath>
+#include <mutex>
+#include <string>
 
 #include "common.cuh"
 #include "scan.cuh"
@@ -741,3 +743,176 @@ int64_t run_partition(cwlb_ctx* ctx, int32_t n_rows, const int32_t* d_rowoff,
 }
 
 }  // namespace cwlb
+
+// ===========================================================================
+// No-allocation variant of the device partitioner.
+//
+// Some callers cannot let a library call cudaMalloc/cudaFree: their device
+// memory belongs to another allocator (a framework's caching allocator, or a
+// pool sized once at start-up by a server that must keep its footprint fixed),
+// and cudaMalloc/cudaFree would also synchronise the device in the middle of
+// their pipelines.  They can still pass input and output buffers.  For them,
+// cwlb_partition_device_noalloc keeps all of its scratch in one file-scope
+// device array of fixed size, g_noalloc_scratch below, which every GPU that
+// loads this library holds until the process exits.  The array is shared by
+// every call and keeps the previous call's contents; nothing in it has to
+// start at zero (each piece is written before it is read).  Calls whose work
+// overlaps on the GPU (two streams, two host threads) race on it and must be
+// serialised by the caller.
+// ===========================================================================
+
+namespace cwlb {
+namespace {
+
+constexpr size_t kNoallocAlign = 256;
+constexpr size_t noalloc_round(size_t b) { return (b + kNoallocAlign - 1) / kNoallocAlign * kNoallocAlign; }
+constexpr size_t kNoallocPosBytes = noalloc_round(sizeof(int32_t) * CWLB_NOALLOC_MAX_ROWS);
+constexpr size_t kNoallocScanBytes = 8192;  // scan tree for <= 2^20 items
+constexpr size_t kNoallocRunBytes = noalloc_round(sizeof(int32_t) * (CWLB_NOALLOC_MAX_RUNS + 1));
+constexpr size_t kNoallocMaxDesc = 4 * static_cast<size_t>(CWLB_NOALLOC_MAX_RUNS) + 16;
+constexpr size_t kNoallocDescBytes = noalloc_round(sizeof(Desc) * kNoallocMaxDesc);
+constexpr size_t kNoallocSmallBytes = 512;  // run count, walker summary, literal count
+constexpr size_t kNoallocBytes =
+    kNoallocPosBytes + kNoallocScanBytes + kNoallocRunBytes + kNoallocDescBytes + kNoallocSmallBytes;
+static_assert(kNoallocBytes <= (8u << 20), "no-allocation scratch exceeds its stated 8 MiB");
+
+// The scratch.  Host code must not use this name as a device address (in host
+// code it is only a stand-in); it uses the address from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[8u << 20];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[256] = {};
+
+// Device address of g_noalloc_scratch on the current device, looked up once
+// per device (the first call on each device; it must precede any stream
+// capture that includes this entry point).
+void* noalloc_scratch_current_device() {
+    int dev = -1;
+    CWLB_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 256) fail(CWLB_ERR_RUNTIME, "device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        CWLB_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        if (!p) fail(CWLB_ERR_CUDA, "cudaGetSymbolAddress returned a null address");
+        g_noalloc_addr[dev] = p;
+    }
+    return g_noalloc_addr[dev];
+}
+
+// run_compact_kernel with a capacity: run starts beyond max_runs are not
+// stored (the host then rejects the input); the run count is always stored.
+__global__ void run_compact_capped_kernel(const int32_t* __restrict__ rowoff, int32_t n,
+                                          const int32_t* __restrict__ pos, int32_t max_runs,
+                                          int32_t* __restrict__ run_start,
+                                          int32_t* __restrict__ n_runs) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int32_t d = rowoff[i + 1] - rowoff[i];
+    const bool start = (i == 0 || d != rowoff[i] - rowoff[i - 1]);
+    if (start && pos[i] < max_runs) run_start[pos[i]] = static_cast<int32_t>(i);
+    if (i == n - 1) {
+        const int32_t r = pos[i] + (start ? 1 : 0);
+        *n_runs = r;
+        if (r <= max_runs) run_start[r] = n;
+    }
+}
+
+int64_t partition_noalloc(cudaStream_t s, int32_t n_rows, const int32_t* d_rowoff,
+                          const cwlb_costs& costs, double capacity, cwlb_task* d_tasks,
+                          int64_t max_tasks) {
+    if (n_rows > CWLB_NOALLOC_MAX_ROWS) {
+        fail(CWLB_ERR_INVALID_ARGUMENT,
+             "cwlb_partition_device_noalloc: " + std::to_string(n_rows) +
+                 " rows exceed the no-allocation scratch limit of " +
+                 std::to_string(CWLB_NOALLOC_MAX_ROWS) + " rows");
+    }
+    char* base = static_cast<char*>(noalloc_scratch_current_device());
+    int32_t* pos = reinterpret_cast<int32_t*>(base);
+    void* scan_tmp = base + kNoallocPosBytes;
+    int32_t* run_start = reinterpret_cast<int32_t*>(base + kNoallocPosBytes + kNoallocScanBytes);
+    Desc* desc = reinterpret_cast<Desc*>(base + kNoallocPosBytes + kNoallocScanBytes + kNoallocRunBytes);
+    char* small = base + kNoallocPosBytes + kNoallocScanBytes + kNoallocRunBytes + kNoallocDescBytes;
+    int32_t* d_R = reinterpret_cast<int32_t*>(small);
+    WalkOut* wout = reinterpret_cast<WalkOut*>(small + 64);
+    int64_t* d_count = reinterpret_cast<int64_t*>(small + 256);
+
+    const Params p = make_params(n_rows, costs, capacity);
+    const bool fast = std::isfinite(p.wCL) && std::isfinite(p.Cs) && std::isfinite(p.Ca) &&
+                      std::isfinite(p.cap) && p.wCL > 0.0;
+    auto literal = [&]() -> int64_t {
+        literal_partition_kernel<<<1, 32, 0, s>>>(p, d_rowoff, d_tasks, max_tasks, d_count);
+        CWLB_LAUNCH_CHECK("literal_partition_kernel");
+        int64_t cnt = 0;
+        CWLB_CUDA(cudaMemcpyAsync(&cnt, d_count, sizeof(cnt), cudaMemcpyDeviceToHost, s));
+        CWLB_CUDA(cudaStreamSynchronize(s));
+        return cnt;
+    };
+    if (!fast) return literal();
+
+    const int64_t n = n_rows;
+    const unsigned blocks = static_cast<unsigned>(ceil_div(n, 256));
+    if (scan_scratch_bytes<int32_t>(n) > kNoallocScanBytes) fail(CWLB_ERR_RUNTIME, "scan scratch");
+    run_flags_kernel<<<blocks, 256, 0, s>>>(d_rowoff, n_rows, pos);
+    CWLB_LAUNCH_CHECK("run_flags_kernel");
+    device_exclusive_scan<int32_t>(pos, pos, n, scan_tmp, s);
+    run_compact_capped_kernel<<<blocks, 256, 0, s>>>(d_rowoff, n_rows, pos, CWLB_NOALLOC_MAX_RUNS,
+                                                     run_start, d_R);
+    CWLB_LAUNCH_CHECK("run_compact_capped_kernel");
+    int32_t R = 0;
+    CWLB_CUDA(cudaMemcpyAsync(&R, d_R, sizeof(R), cudaMemcpyDeviceToHost, s));
+    CWLB_CUDA(cudaStreamSynchronize(s));
+    if (R > CWLB_NOALLOC_MAX_RUNS) {
+        fail(CWLB_ERR_INVALID_ARGUMENT,
+             "cwlb_partition_device_noalloc: " + std::to_string(R) +
+                 " distinct row degrees exceed the no-allocation scratch limit of " +
+                 std::to_string(CWLB_NOALLOC_MAX_RUNS));
+    }
+    walk_kernel<<<1, kWalkThreads, 0, s>>>(p, d_rowoff, run_start, d_R, desc, wout);
+    CWLB_LAUNCH_CHECK("walk_kernel");
+    WalkOut w{};
+    CWLB_CUDA(cudaMemcpyAsync(&w, wout, sizeof(w), cudaMemcpyDeviceToHost, s));
+    CWLB_CUDA(cudaStreamSynchronize(s));
+    if (w.fallback) return literal();
+    if (w.n_tasks > max_tasks || w.n_tasks <= 0) return w.n_tasks;
+    expand_kernel<<<static_cast<unsigned>(ceil_div(w.n_tasks, 256)), 256, 0, s>>>(p, desc, w.n_desc,
+                                                                                  w.n_tasks, d_tasks);
+    CWLB_LAUNCH_CHECK("expand_kernel");
+    return w.n_tasks;
+}
+
+}  // namespace
+}  // namespace cwlb
+
+extern "C" int cwlb_partition_device_noalloc(void* cuda_stream, int32_t n_rows,
+                                             const int32_t* d_row_offset, const cwlb_costs* costs,
+                                             double capacity, cwlb_task* d_tasks,
+                                             int64_t max_tasks, int64_t* n_tasks) {
+    try {
+        if (!costs || !n_tasks || (n_rows > 0 && !d_row_offset) || max_tasks < 0) {
+            cwlb::fail(CWLB_ERR_INVALID_ARGUMENT, "cwlb_partition_device_noalloc: null argument");
+        }
+        *n_tasks = 0;
+        if (n_rows <= 0) return CWLB_OK;
+        const int64_t cnt = cwlb::partition_noalloc(static_cast<cudaStream_t>(cuda_stream), n_rows,
+                                                    d_row_offset, *costs, capacity, d_tasks,
+                                                    max_tasks);
+        *n_tasks = cnt;
+        if (cnt > max_tasks) {
+            cwlb::fail(CWLB_ERR_BUFFER_TOO_SMALL,
+                       "cwlb_partition_device_noalloc: the task buffer holds " +
+                           std::to_string(max_tasks) + " tasks, " + std::to_string(cnt) +
+                           " are needed");
+        }
+        if (cnt > 0 && !d_tasks) {
+            cwlb::fail(CWLB_ERR_INVALID_ARGUMENT, "cwlb_partition_device_noalloc: null task buffer");
+        }
+        return CWLB_OK;
+    } catch (const cwlb::Failure& e) {
+        cwlb::set_last_error(e.what());
+        return e.code;
+    } catch (const std::exception& e) {
+        cwlb::set_last_error(e.what());
+        return CWLB_ERR_RUNTIME;
+    }
+}

@@ -189,6 +189,31 @@ int cwlb_partition_device(cwlb_ctx* ctx, int32_t n_rows, const int32_t* d_row_of
                           const cwlb_costs* costs, double capacity, cwlb_task** d_tasks,
                           int64_t* n_tasks);
 
+/* Device partitioner that allocates nothing.  It has no counterpart in the
+ * reference.  It is for callers that cannot let a library call cudaMalloc or
+ * cudaFree: their device memory is owned by another allocator (a framework's
+ * caching allocator, or a pool a server sizes once at start-up to keep its
+ * footprint fixed), and those calls would also synchronise the device in the
+ * middle of their pipelines.  Such callers pass the input offsets and the
+ * output task buffer; the scratch lives in one fixed 8 MiB device array that
+ * every GPU loading this library holds until the process exits.
+ * Same result as cwlb_partition_device (bit-identical task list), written to
+ * d_tasks (capacity max_tasks; CWLB_ERR_BUFFER_TOO_SMALL with *n_tasks set
+ * when it does not fit).  Limits: n_rows <= CWLB_NOALLOC_MAX_ROWS and at most
+ * CWLB_NOALLOC_MAX_RUNS distinct row degrees; larger inputs are rejected with
+ * CWLB_ERR_INVALID_ARGUMENT.  Runs on `cuda_stream` (a cudaStream_t; NULL is
+ * the default stream) of the calling thread's current device, needs no
+ * context, and synchronises that stream twice to learn sizes.  The first call
+ * on each device looks up the scratch array's device address; make that first
+ * call before any stream capture that includes this function.  All calls share
+ * the one array: calls whose work overlaps on the GPU race and must be
+ * serialised by the caller. */
+#define CWLB_NOALLOC_MAX_ROWS 1048576
+#define CWLB_NOALLOC_MAX_RUNS 16384
+int cwlb_partition_device_noalloc(void* cuda_stream, int32_t n_rows, const int32_t* d_row_offset,
+                                  const cwlb_costs* costs, double capacity, cwlb_task* d_tasks,
+                                  int64_t max_tasks, int64_t* n_tasks);
+
 /* ----------------------------------------------------- S-selection helpers */
 
 /* capacity_from_s (main.cpp:281-292). */
