@@ -40,6 +40,7 @@ for _p in (os.path.join(ROOT, "cwlb-spmm_b200"), os.path.join(ROOT, "oracle")):
         sys.path.insert(0, _p)
 
 import graphs  # noqa: E402
+import shards  # noqa: E402
 
 # Cost weights used to partition (ns x 10 per operation, spmm_costs.txt order).
 COSTS_FILE = os.path.join(ROOT, "cwlb-spmm_b200", "resources", "spmm_costs.txt")
@@ -75,6 +76,16 @@ def read_costs():
     if c is None:
         raise RuntimeError(f"cannot read {COSTS_FILE}")
     return c
+
+
+def measured_traffic(workload):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu
+    summary (profiles/traffic.json), or None for workloads not captured."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f)[workload]["bytes_per_launch"]
+    except Exception:
+        return None
 
 
 def hbm_peak():
@@ -179,32 +190,11 @@ def barrier(world):
 # ---------------------------------------------------------------------------
 # workload
 
-def shard_bounds(rowoff_t, costs, world, rank):
-    """Contiguous block of original rows with ~1/world of the total cost
-    (full_w = (Cc + Cl) deg + Cs per row)."""
-    import torch
-    if world == 1:
-        return 0, rowoff_t.numel() - 1
-    deg = (rowoff_t[1:] - rowoff_t[:-1]).to(torch.float64)
-    w = deg * (costs.C_compute_ns + costs.C_load_ns) + costs.C_store_ns
-    cum = torch.cumsum(w, 0)
-    total = float(cum[-1])
-    n = deg.numel()
-
-    def cut(k):
-        if k == 0:
-            return 0
-        if k == world:
-            return n
-        return int(torch.searchsorted(cum, total * k / world).item()) + 1
-
-    return min(cut(rank), n), min(cut(rank + 1), n)
-
-
 def build_workload(cfg_id, device, world, rank, costs, scale_down=1):
     import torch
     rowoff, col, val, X = graphs.build_config_torch(cfg_id, device, scale_down=scale_down)
-    a, b = shard_bounds(rowoff, costs, world, rank)
+    a, b = shards.shard_bounds(rowoff, costs.C_compute_ns + costs.C_load_ns, costs.C_store_ns,
+                               world, rank)
     e0, e1 = int(rowoff[a]), int(rowoff[b])
     ro = (rowoff[a:b + 1] - e0).contiguous()
     sub_col = col[e0:e1].contiguous()
@@ -283,6 +273,9 @@ def compulsory_bytes(n, nnz, n_tasks, K, x_rows):
 # CPU baseline: the oracle (restatement of the reference's kernel semantics)
 
 def cpu_baseline(wl, tasks_np, target_seconds):
+    """Time the oracle's OpenMP aggregation on this host: a contiguous slice of
+    the task list (the whole list when it is short), repeated until about
+    `target_seconds` of CPU work has been timed."""
     from oracle import Oracle
     oracle = Oracle()
     srow = wl["sro"].cpu().numpy()
@@ -292,8 +285,8 @@ def cpu_baseline(wl, tasks_np, target_seconds):
     X = wl["X"].cpu().numpy()
     K = wl["K"]
     threads = os.cpu_count() or 1
-    # nnz covered by a contiguous slice of tasks starting in the middle of the list
     task_nnz = _task_nnz(srow, tasks_np)
+    n_t = len(tasks_np)
 
     def run(t0, t1):
         sub = np.ascontiguousarray(tasks_np[t0:t1])
@@ -301,20 +294,27 @@ def cpu_baseline(wl, tasks_np, target_seconds):
         oracle.spmm_mean(srow, scol, sval, org, X, sub, n_threads=threads)
         return time.perf_counter() - s, int(task_nnz[t0:t1].sum())
 
-    n_t = len(tasks_np)
+    # probe ~1% of the tasks to size a slice of ~target/4 seconds
     start = n_t // 3
-    probe = max(1, min(n_t - start, n_t // 200 + 1))
+    probe = max(1, min(n_t - start, n_t // 100 + 1))
     dt, nz = run(start, start + probe)
     rate = max(nz, 1) / max(dt, 1e-6)
-    want_nnz = rate * target_seconds
-    csum = np.cumsum(task_nnz[start:])
-    t1 = start + int(np.searchsorted(csum, want_nnz)) + 1
-    t1 = min(max(t1, start + 1), n_t)
-    dt, nz = run(start, t1)
-    return {"value": 2.0 * nz * K / dt / 1e9, "unit": "GFLOP/s", "cores": threads,
+    csum = np.cumsum(task_nnz)
+    want = rate * target_seconds / 4
+    t0 = start if csum[-1] - csum[start] > want else 0
+    base = csum[t0 - 1] if t0 > 0 else 0
+    t1 = min(n_t, int(np.searchsorted(csum, base + want)) + 1)
+    tot_t, tot_nz, reps = 0.0, 0, 0
+    while tot_t < target_seconds and reps < 1000:
+        dt, nz = run(t0, t1)
+        tot_t += dt
+        tot_nz += nz
+        reps += 1
+    return {"value": 2.0 * tot_nz * K / tot_t / 1e9, "unit": "GFLOP/s", "cores": threads,
             "kind": "port",
-            "sample": f"oracle spmm_mean over tasks [{start}, {t1}) = {nz} nnz of {wl['nnz']} "
-                      f"(K={K}), {dt:.1f} s, {threads} OpenMP threads"}
+            "sample": f"oracle spmm_mean over tasks [{t0}, {t1}) = {tot_nz // reps} of "
+                      f"{wl['nnz']} nnz (K={K}), repeated {reps}x, {tot_t:.1f} s, "
+                      f"{threads} OpenMP threads"}
 
 
 def _task_nnz(srow, tasks):
@@ -440,7 +440,9 @@ def run_ours(args):
                        "hbm_gbs_rank0": round(achieved, 1)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_source": peak_kind, "traffic": None,
+                         "peak_source": peak_kind,
+                         "traffic": measured_traffic(f"config {args.config}: {cfg['name']}")
+                         if args.scale_down == 1 and world == 1 else None,
                          "algorithmic_bytes_per_launch": bytes_local,
                          "launch_us": round(per_launch * 1e6, 2)},
             "e2e": e2e,
@@ -485,7 +487,7 @@ def run_reference(args):
     wl = dict(sro=torch.from_numpy(srow), scol=torch.from_numpy(scol),
               sval=torch.from_numpy(sval), org=torch.from_numpy(origin), X=torch.from_numpy(X),
               K=K, nnz=nnz, n=len(origin))
-    per_step = max(1.0, 150.0 / max(args.steps + args.warmup, 1))
+    per_step = min(15.0, max(0.5, 120.0 / max(args.steps + args.warmup, 1)))
     for _ in range(args.warmup):
         cpu_baseline(wl, tasks, min(per_step, 2.0))
     vals, samples = [], []

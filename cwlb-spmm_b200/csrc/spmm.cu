@@ -379,34 +379,57 @@ __global__ void __launch_bounds__(kThreads) spmm_scalar_kernel(SpmmArgs a) {
 // ---------------------------------------------------------------------------
 // Rows-covered mode: zero exactly the output rows that are assembled from
 // fragments (each such row has one fragment starting at offset 0), before the
-// aggregation kernel adds into them.  One warp per task.
+// aggregation kernel adds into them.  One thread checks one task; the warp
+// then zeroes the flagged rows together with coalesced stores.
+
+__device__ __forceinline__ int32_t first_fragment_row(const SpmmArgs& a, const cwlb_task& tk,
+                                                      int r) {
+    // Returns origin[r] if row r's fragment in this task starts at 0 and does
+    // not cover the whole row; -1 otherwise.
+    const int32_t b0 = __ldg(a.rowoff + r);
+    const int32_t b1 = __ldg(a.rowoff + r + 1);
+    if (b0 < 0 || b1 < b0 || b1 > a.nnz) return -1;
+    const int32_t deg = b1 - b0;
+    if (deg <= 0) return -1;
+    int32_t begin = (r == tk.row_start) ? tk.first_row_offset : 0;
+    int32_t end = deg;
+    if (r == tk.row_end - 1 && tk.last_row_nnz > 0) end = tk.last_row_nnz;
+    begin = min(max(begin, 0), deg);
+    end = min(max(end, begin), deg);
+    if (!(begin == 0 && end > 0 && end < deg)) return -1;
+    const int32_t o = __ldg(a.origin + r);
+    return (o >= 0 && o < a.n_rows) ? o : -1;
+}
 
 __global__ void __launch_bounds__(kThreads) zero_split_rows_kernel(SpmmArgs a) {
     const int lane = threadIdx.x & 31;
-    const int64_t t = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
-    if (t >= a.n_tasks) return;
-    const cwlb_task tk{__ldg(&a.tasks[t].row_start), __ldg(&a.tasks[t].row_end),
-                       __ldg(&a.tasks[t].first_row_offset), __ldg(&a.tasks[t].last_row_nnz)};
-    if (tk.row_start < 0 || tk.row_end > a.n_rows || tk.row_start >= tk.row_end) return;
-    const int rows[2] = {tk.row_start, tk.row_end - 1};
-    const int n = rows[0] == rows[1] ? 1 : 2;
-    for (int i = 0; i < n; ++i) {
-        const int r = rows[i];
-        const int32_t b0 = __ldg(a.rowoff + r);
-        const int32_t b1 = __ldg(a.rowoff + r + 1);
-        if (b0 < 0 || b1 < b0 || b1 > a.nnz) continue;
-        const int32_t deg = b1 - b0;
-        if (deg <= 0) continue;
-        int32_t begin = (r == tk.row_start) ? tk.first_row_offset : 0;
-        int32_t end = deg;
-        if (r == tk.row_end - 1 && tk.last_row_nnz > 0) end = tk.last_row_nnz;
-        begin = min(max(begin, 0), deg);
-        end = min(max(end, begin), deg);
-        if (!(begin == 0 && end > 0 && end < deg)) continue;
-        const int32_t o = __ldg(a.origin + r);
-        if (o < 0 || o >= a.n_rows) continue;
-        float* orow = a.out + static_cast<int64_t>(o) * a.K;
-        for (int64_t k = lane; k < a.K; k += 32) orow[k] = 0.0f;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    int32_t rows_to_zero[2] = {-1, -1};
+    if (t < a.n_tasks) {
+        const cwlb_task tk{__ldg(&a.tasks[t].row_start), __ldg(&a.tasks[t].row_end),
+                           __ldg(&a.tasks[t].first_row_offset), __ldg(&a.tasks[t].last_row_nnz)};
+        if (tk.row_start >= 0 && tk.row_end <= a.n_rows && tk.row_start < tk.row_end) {
+            rows_to_zero[0] = first_fragment_row(a, tk, tk.row_start);
+            if (tk.row_end - 1 != tk.row_start)
+                rows_to_zero[1] = first_fragment_row(a, tk, tk.row_end - 1);
+        }
+    }
+    const bool vec = (a.K % 4 == 0) && (reinterpret_cast<uintptr_t>(a.out) % 16 == 0);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        unsigned pending = __ballot_sync(0xffffffffu, rows_to_zero[i] >= 0);
+        while (pending) {
+            const int src = __ffs(pending) - 1;
+            pending &= pending - 1;
+            const int32_t o = __shfl_sync(0xffffffffu, rows_to_zero[i], src);
+            if (vec) {
+                float4* row = reinterpret_cast<float4*>(a.out) + static_cast<int64_t>(o) * (a.K >> 2);
+                for (int64_t k = lane; k < (a.K >> 2); k += 32) row[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {
+                float* row = a.out + static_cast<int64_t>(o) * a.K;
+                for (int64_t k = lane; k < a.K; k += 32) row[k] = 0.0f;
+            }
+        }
     }
 }
 
@@ -481,7 +504,7 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
     a.write_empty = covered ? 1 : 0;
 
     if (covered) {
-        dim3 grid(static_cast<unsigned>(ceil_div(n_tasks, kWarpsPerCta)));
+        dim3 grid(static_cast<unsigned>(ceil_div(n_tasks, kThreads)));
         zero_split_rows_kernel<<<grid, kThreads, 0, s>>>(a);
         CWLB_LAUNCH_CHECK("zero_split_rows_kernel");
     }

@@ -1,0 +1,59 @@
+"""Row shards for running the aggregation on several GPUs of one node.
+
+The path partitions without a data exchange: each rank takes a contiguous
+block of ORIGINAL rows [a, b) whose summed full-row weight
+(Cc + Cl) * deg + Cs -- the weight the reference's partitioner gives a whole
+row (src/utils.cpp:850-852) -- is about 1/world of the total, sorts and
+partitions that block on its own GPU, and aggregates it with the dense input
+replicated.  Its output rows are a contiguous slice of the original-order
+output, so no collective touches the data path.
+"""
+from __future__ import annotations
+
+
+def shard_bounds(rowoff, edge_weight: float, store_weight: float, world: int, rank: int):
+    """[a, b) of rank `rank` out of `world`: cuts where the prefix sum of
+    edge_weight * deg + store_weight crosses k/world of the total.  Works on a
+    torch tensor or a numpy array of row offsets (int, length rows + 1)."""
+    n = len(rowoff) - 1
+    if world <= 1:
+        return 0, n
+    try:
+        import torch
+        is_torch = isinstance(rowoff, torch.Tensor)
+    except ImportError:  # pragma: no cover
+        is_torch = False
+    if is_torch:
+        import torch
+        deg = (rowoff[1:] - rowoff[:-1]).to(torch.float64)
+        cum = torch.cumsum(deg * edge_weight + store_weight, 0)
+        total = float(cum[-1]) if n else 0.0
+
+        def cut(k):
+            if k <= 0:
+                return 0
+            if k >= world:
+                return n
+            return int(torch.searchsorted(cum, total * k / world).item()) + 1
+    else:
+        import numpy as np
+        deg = np.diff(np.asarray(rowoff, dtype=np.int64)).astype(np.float64)
+        cum = np.cumsum(deg * edge_weight + store_weight)
+        total = float(cum[-1]) if n else 0.0
+
+        def cut(k):
+            if k <= 0:
+                return 0
+            if k >= world:
+                return n
+            return int(np.searchsorted(cum, total * k / world)) + 1
+
+    return min(cut(rank), n), min(cut(rank + 1), n)
+
+
+def shard_csr(rowoff, col, val, a: int, b: int):
+    """The sub-CSR of original rows [a, b): rebased offsets, column ids and
+    values (columns still index the full, replicated dense input)."""
+    e0, e1 = int(rowoff[a]), int(rowoff[b])
+    ro = rowoff[a:b + 1] - e0
+    return ro, col[e0:e1], val[e0:e1]
