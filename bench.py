@@ -153,6 +153,15 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def physical_gpus(logical):
+    """nvidia-smi indices of the given CUDA device ordinals."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [v.strip() for v in vis.split(",") if v.strip()]
+    if ids and all(v.isdigit() for v in ids):
+        return [int(ids[i]) if i < len(ids) else i for i in logical]
+    return logical
+
+
 # ---------------------------------------------------------------------------
 # distributed plumbing
 
@@ -373,7 +382,8 @@ def run_ours(args):
     for _ in range(args.warmup):
         run_step(ctx, wl, tasks, n_tasks, out, flags)
     torch.cuda.synchronize()
-    sampler = ClockSampler(list(range(world)) if world > 1 else [local]) if rank == 0 else None
+    sampler = ClockSampler(physical_gpus(list(range(world)) if world > 1 else [local])) \
+        if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)

@@ -384,6 +384,19 @@ int cwlb_partition_device(cwlb_ctx* ctx, int32_t n_rows, const int32_t* d_row_of
     });
 }
 
+int cwlb_measure_spmm_costs(cwlb_ctx* ctx, int32_t K, int32_t repeat, int32_t WI,
+                            int32_t data_MB_for_load, int32_t atomic_target_writers,
+                            cwlb_costs* out) {
+    return guarded([&] {
+        check_ctx(ctx);
+        require(out != nullptr, CWLB_ERR_INVALID_ARGUMENT, "null output");
+        if (K <= 0 || repeat <= 0 || WI <= 0 || data_MB_for_load <= 0 || atomic_target_writers <= 0) {
+            cwlb::fail(CWLB_ERR_INVALID_ARGUMENT, "All microbenchmark parameters must be positive.");
+        }
+        cwlb::measure_costs(ctx, K, repeat, WI, data_MB_for_load, atomic_target_writers, out);
+    });
+}
+
 // ---------------------------------------------------------------------------
 // Host-side helpers (scalar arithmetic the reference also does on the host).
 

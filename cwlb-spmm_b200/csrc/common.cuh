@@ -88,6 +88,9 @@ void launch_sort_by_degree(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int
 // Returns the number of tasks; the tasks are in ctx->part_tasks.
 int64_t run_partition(cwlb_ctx* ctx, int32_t n_rows, const int32_t* d_rowoff,
                       const cwlb_costs& costs, double capacity);
+// The four calibration microbenchmarks (calibrate.cu).
+void measure_costs(cwlb_ctx* ctx, int K, int repeat, int WI, int data_MB, int writers,
+                   cwlb_costs* out);
 // Sets the calling thread's cwlb_last_error() message (defined in capi.cu).
 void set_last_error(const std::string& msg);
 

@@ -105,6 +105,7 @@ _sig("cwlb_segment_size", [C.POINTER(cwlb_costs), _dbl], _i32)
 _sig("cwlb_wave_based_s", [_i64, _i32, _i32, C.POINTER(_i32)])
 _sig("cwlb_recommended_candidate_w", [C.c_uint64, C.POINTER(_i32)], None)
 _sig("cwlb_save_costs", [C.POINTER(cwlb_costs), C.c_char_p, _i32, _i32])
+_sig("cwlb_measure_spmm_costs", [_vp, _i32, _i32, _i32, _i32, _i32, C.POINTER(cwlb_costs)])
 _sig("cwlb_read_costs", [C.POINTER(cwlb_costs), C.c_char_p])
 
 
@@ -307,6 +308,15 @@ class Context:
             _check(_lib.cwlb_partition(self._h, n, _p(csr.RowOffset), C.byref(c),
                                        float(capacity_weight), _p(out), cnt.value, C.byref(cnt)))
         return out
+
+    def measure_spmm_costs(self, K=128, repeat=500, WI=131072, data_MB_for_load=512,
+                           atomic_target_writers=8) -> "SpmmCostParams":
+        """measure_spmm_costs (include/utils.h:47-54): the costWrite calibration."""
+        c = cwlb_costs()
+        _check(_lib.cwlb_measure_spmm_costs(self._h, K, repeat, WI, data_MB_for_load,
+                                            atomic_target_writers, C.byref(c)))
+        return SpmmCostParams(c.C_compute_ns, c.C_load_ns, c.C_store_ns, c.C_atomic_ns, c.K,
+                              c.WI, c.repeat, c.atomic_writers_per_addr)
 
     # ---- device-pointer entry points (asynchronous on the context stream) --
 

@@ -1,0 +1,237 @@
+// Interface functions of include/utils.h over libcwlb_spmm.
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <iomanip>
+#include <iostream>
+#include <limits>
+#include <stdexcept>
+
+#include "utils.h"
+
+static_assert(sizeof(ParallelDataWeighted) == sizeof(cwlb_task), "task layout");
+
+namespace {
+cwlb_costs to_c(const SpmmCostParams& p) {
+    cwlb_costs c{};
+    c.C_compute_ns = p.C_compute_ns;
+    c.C_load_ns = p.C_load_ns;
+    c.C_store_ns = p.C_store_ns;
+    c.C_atomic_ns = p.C_atomic_ns;
+    c.K = p.K;
+    c.WI = p.WI;
+    c.repeat = p.repeat;
+    c.atomic_writers_per_addr = p.atomic_writers_per_addr;
+    return c;
+}
+}  // namespace
+
+CSR::CSR(const Defined::RowMajorMatrixXf& adj) {
+    if (adj.rows() != adj.cols()) throw std::invalid_argument("Adjacency matrix must be square");
+    int count = 0;
+    for (long i = 0; i < adj.rows(); ++i) {
+        RowOffset.push_back(count);
+        for (long j = 0; j < adj.cols(); ++j) {
+            if (adj(i, j) != 0) {
+                ColInd.push_back(static_cast<int>(j));
+                Value.push_back(adj(i, j));
+                ++count;
+            }
+        }
+    }
+    RowOffset.push_back(count);
+}
+
+CSR_Order sortCSRByDegree(const CSR& csr, cwlb::Queue& q) {
+    CSR_Order out;
+    if (csr.RowOffset.size() < 2) return out;
+    if (csr.ColInd.size() != csr.Value.size()) {
+        throw std::runtime_error("CSR ColInd and Value size mismatch.");
+    }
+    const std::size_t rows = csr.RowOffset.size() - 1;
+    if (rows > static_cast<std::size_t>(std::numeric_limits<int>::max()) ||
+        csr.ColInd.size() > static_cast<std::size_t>(std::numeric_limits<int>::max())) {
+        throw std::overflow_error(
+            "DPL CPU degree reordering requires row and NNZ counts to fit in int.");
+    }
+    const int n = static_cast<int>(rows);
+    const int nnz = static_cast<int>(csr.ColInd.size());
+    out.Origin_local.resize(rows);
+    out.RowOffset.resize(rows + 1);
+    out.ColInd.resize(csr.ColInd.size());
+    out.Value.resize(csr.Value.size());
+    cwlb::check(cwlb_sort_by_degree(q.ctx(), n, nnz, csr.RowOffset.data(), csr.ColInd.data(),
+                                    csr.Value.data(), out.Origin_local.data(), out.RowOffset.data(),
+                                    out.ColInd.data(), out.Value.data()));
+    return out;
+}
+
+SpmmCostParams measure_spmm_costs(cwlb::Queue& q, int K, int repeat, int WI, int data_MB_for_load,
+                                  int atomic_target_writers, const std::vector<int>&) {
+    cwlb_costs c{};
+    cwlb::check(cwlb_measure_spmm_costs(q.ctx(), K, repeat, WI, data_MB_for_load,
+                                        atomic_target_writers, &c));
+    SpmmCostParams p;
+    p.C_compute_ns = c.C_compute_ns;
+    p.C_load_ns = c.C_load_ns;
+    p.C_store_ns = c.C_store_ns;
+    p.C_atomic_ns = c.C_atomic_ns;
+    p.K = c.K;
+    p.WI = c.WI;
+    p.repeat = c.repeat;
+    p.atomic_writers_per_addr = c.atomic_writers_per_addr;
+    return p;
+}
+
+std::vector<ParallelDataWeighted> costWeightedTaskPartitioning(cwlb::Queue& q,
+                                                               const CSR_Order& csr,
+                                                               const SpmmCostParams& costs,
+                                                               double capacity_weight) {
+    std::vector<ParallelDataWeighted> tasks;
+    const int n = static_cast<int>(csr.RowOffset.size()) - 1;
+    if (n <= 0) return tasks;
+    const cwlb_costs c = to_c(costs);
+    int64_t cnt = 0;
+    // First call: the task count; second call: the task list.
+    cwlb::check(cwlb_partition(q.ctx(), n, csr.RowOffset.data(), &c, capacity_weight, nullptr, 0, &cnt));
+    tasks.resize(static_cast<std::size_t>(cnt));
+    if (cnt > 0) {
+        cwlb::check(cwlb_partition(q.ctx(), n, csr.RowOffset.data(), &c, capacity_weight,
+                                   reinterpret_cast<cwlb_task*>(tasks.data()), cnt, &cnt));
+    }
+    return tasks;
+}
+
+std::vector<ParallelDataWeighted> costWeightedTaskPartitioning(const CSR_Order& csr,
+                                                               const SpmmCostParams& costs,
+                                                               double capacity_weight) {
+    return costWeightedTaskPartitioning(cwlb::Queue::thread_default(), csr, costs, capacity_weight);
+}
+
+bool save_costs_one_per_line(SpmmCostParams costs, const std::string& filepath, bool append,
+                             int precision) {
+    const cwlb_costs c = to_c(costs);
+    return cwlb_save_costs(&c, filepath.c_str(), append ? 1 : 0, precision) == CWLB_OK;
+}
+
+bool read_costs_one_per_line(SpmmCostParams& out, const std::string& filepath) {
+    cwlb_costs c{};
+    if (cwlb_read_costs(&c, filepath.c_str()) != CWLB_OK) return false;
+    out.C_compute_ns = c.C_compute_ns;
+    out.C_load_ns = c.C_load_ns;
+    out.C_store_ns = c.C_store_ns;
+    out.C_atomic_ns = c.C_atomic_ns;
+    return true;
+}
+
+std::vector<std::pair<int, float>> get_csr_row_elements(const CSR& csr, int row) {
+    std::vector<std::pair<int, float>> e;
+    const int rows = static_cast<int>(csr.RowOffset.size()) - 1;
+    if (row < 0 || row >= rows) return e;
+    for (int i = csr.RowOffset[row]; i < csr.RowOffset[row + 1]; ++i) {
+        e.emplace_back(csr.ColInd[i], csr.Value[i]);
+    }
+    return e;
+}
+
+bool validate_custom_csr_result(const Defined::RowMajorMatrixXf& result,
+                                const Defined::RowMajorMatrixXf& reference, const CSR& csr,
+                                const Defined::RowMajorMatrixXf& dense, float abs_tolerance) {
+    try {
+        if (abs_tolerance < 0.0f || !std::isfinite(abs_tolerance)) {
+            throw std::invalid_argument("Validation tolerance must be finite and non-negative.");
+        }
+        if (result.rows() != reference.rows() || result.cols() != reference.cols()) {
+            std::cerr << "Validation failed: result matrix shape is (" << result.rows() << ", "
+                      << result.cols() << "), but reference matrix shape is ("
+                      << reference.rows() << ", " << reference.cols() << ").\n";
+            return false;
+        }
+        if (csr.RowOffset.size() != static_cast<std::size_t>(reference.rows()) + 1) {
+            std::cerr << "Validation failed: CSR row count does not match the reference matrix.\n";
+            return false;
+        }
+        if (dense.rows() <= 0 || dense.cols() != reference.cols()) {
+            std::cerr << "Validation failed: input dense matrix shape is incompatible with the "
+                         "reference result.\n";
+            return false;
+        }
+        std::vector<ErrorElement> errors;
+        for (long r = 0; r < reference.rows() && errors.size() < 10; ++r) {
+            for (long c = 0; c < reference.cols() && errors.size() < 10; ++c) {
+                const float got = result(r, c), want = reference(r, c);
+                bool bad;
+                float err;
+                if (std::isnan(got) || std::isnan(want)) {
+                    bad = !(std::isnan(got) && std::isnan(want));
+                    err = bad ? std::numeric_limits<float>::infinity() : 0.0f;
+                } else if (std::isinf(got) || std::isinf(want)) {
+                    bad = got != want;
+                    err = bad ? std::numeric_limits<float>::infinity() : 0.0f;
+                } else {
+                    err = std::abs(got - want);
+                    bad = err > abs_tolerance;
+                }
+                if (!bad) continue;
+                ErrorElement e;
+                e.result_row = static_cast<int>(r);
+                e.result_col = static_cast<int>(c);
+                e.sycl_value = got;
+                e.reference_value = want;
+                e.absolute_error = err;
+                e.csr_row_elements = get_csr_row_elements(csr, static_cast<int>(r));
+                for (long d = 0; d < dense.rows(); ++d) e.dense_col_elements.push_back(dense(d, c));
+                errors.push_back(std::move(e));
+            }
+        }
+        if (errors.empty()) {
+            std::cout << "\033[1;32mValidation passed: all elements satisfy the comparison "
+                         "criteria.\033[0m\n";
+            return true;
+        }
+        std::cout << "\033[1;31mValidation failed: showing " << errors.size()
+                  << " mismatched elements (up to the first 10).\033[0m\n";
+        for (std::size_t i = 0; i < errors.size(); ++i) {
+            const ErrorElement& e = errors[i];
+            std::cout << "\nStored entries in CSR row " << e.result_row << ":\n"
+                      << "RowOffset[" << e.result_row << "]: " << csr.RowOffset[e.result_row] << '\n'
+                      << "RowOffset[" << e.result_row + 1 << "]: " << csr.RowOffset[e.result_row + 1]
+                      << '\n'
+                      << "Format: [ColInd] -> Value\n";
+            for (const auto& el : e.csr_row_elements) {
+                std::cout << "  [" << el.first << "] -> " << el.second << '\n';
+            }
+            std::cout << "\nDense matrix column " << e.result_col << " (up to the first 5 rows):\n";
+            const int shown = std::min<int>(5, static_cast<int>(e.dense_col_elements.size()));
+            for (int d = 0; d < shown; ++d) {
+                std::cout << "  Row " << d << ": " << e.dense_col_elements[d] << '\n';
+            }
+            std::cout << "\n\033[1;34mMismatch #" << i + 1 << ":\033[0m\n"
+                      << "Result matrix position: (" << e.result_row << ", " << e.result_col << ")\n"
+                      << std::fixed << std::setprecision(6) << "SYCL result:     " << e.sycl_value
+                      << '\n'
+                      << "Reference value: " << e.reference_value << '\n'
+                      << "Absolute error:  " << e.absolute_error << '\n';
+        }
+        return false;
+    } catch (const std::exception& e) {
+        std::cerr << "Validation error: " << e.what() << '\n';
+        return false;
+    }
+}
+
+double capacity_from_s(int s, const SpmmCostParams& costs) {
+    const cwlb_costs c = to_c(costs);
+    return cwlb_capacity_from_s(s, &c);
+}
+
+int wave_based_s(const CSR_Order& sorted_csr, int compute_units, int wave) {
+    if (compute_units <= 0 || wave <= 0) {
+        throw std::invalid_argument("compute_units and wave must be positive.");
+    }
+    if (sorted_csr.RowOffset.empty()) return 1;
+    int32_t s = 0;
+    cwlb::check(cwlb_wave_based_s(static_cast<int64_t>(sorted_csr.RowOffset.back()), compute_units,
+                                  wave, &s));
+    return s;
+}

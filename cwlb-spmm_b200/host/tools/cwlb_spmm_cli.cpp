@@ -1,0 +1,445 @@
+// cwlb-spmm: the command-line driver of the CWLB-SpMM hot path on B200.
+//
+// Same command lines, checks, messages and output lines as the reference's
+// cwlb-spmm (main.cpp:431-741):
+//   cwlb-spmm <dataset> <K> <wave>                    S from the wave count
+//   cwlb-spmm <dataset> <K> --S <S>                   fixed S
+//   cwlb-spmm <dataset> <K> <S_begin> <S_max> <S_step> S sweep, appended to results
+//   cwlb-spmm <dataset> <K> --candidates              three wave-based S values
+//   cwlb-spmm <dataset> <K> --candidate-search [count] | --step <step>
+// Paths default to the reference's (../resources/...), overridable with
+// CWLB_DATASET_DIR, CWLB_COSTFILE and CWLB_RESULTS; CWLB_DEVICE picks the GPU.
+//
+// Each S run partitions on the GPU, uploads the reordered CSR, X and the tasks
+// once, and times LOOPCOUNT aggregation launches with CUDA events (the first
+// WARMUPCOUNT are warm-up), reporting the mean of the timed ones in
+// microseconds, as the reference's event-profiled loop does (main.cpp:338-412).
+#include <algorithm>
+#include <array>
+#include <cctype>
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+#include <fstream>
+#include <iomanip>
+#include <iostream>
+#include <limits>
+#include <random>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "config.h"
+#include "cwlb_queue.h"
+#include "data.h"
+#include "parallelMatrix.h"
+#include "utils.h"
+
+namespace {
+
+constexpr int kMaxSearchPoints = 10000;
+
+std::string env_or(const char* name, const std::string& fallback) {
+    const char* v = std::getenv(name);
+    return v ? std::string(v) : fallback;
+}
+
+std::string cost_path() { return env_or("CWLB_COSTFILE", COSTFILEPATH); }
+std::string results_path() { return env_or("CWLB_RESULTS", "../resources/results.txt"); }
+
+std::array<int, 3> candidate_waves(uint64_t nnz) {
+    int32_t w[3];
+    cwlb_recommended_candidate_w(nnz, w);
+    return {w[0], w[1], w[2]};
+}
+
+int positive_count(const std::string& text) {
+    std::size_t used = 0;
+    const int v = std::stoi(text, &used);
+    if (used != text.size() || v <= 0) {
+        throw std::invalid_argument("Search count/step must be a positive integer.");
+    }
+    return v;
+}
+
+// The neighbourhood around the best of three ascending S candidates.
+std::pair<int, int> search_interval(const std::array<int, 3>& s, std::size_t best) {
+    if (best >= s.size() || s[0] <= 0 || s[1] < s[0] || s[2] < s[1]) {
+        throw std::invalid_argument("Invalid ordered candidate values or best index.");
+    }
+    int64_t lo = s[0], hi = s[2];
+    if (best == 0) {
+        lo = 2LL * s[0] - s[1];
+        hi = s[1];
+    } else if (best == 2) {
+        lo = s[1];
+        hi = 2LL * s[2] - s[1];
+    }
+    lo = std::max<int64_t>(1, lo);
+    hi = std::min<int64_t>(std::numeric_limits<int>::max(), hi);
+    return {static_cast<int>(lo), static_cast<int>(hi)};
+}
+
+std::vector<int> grid_by_count(int lo, int hi, int requested) {
+    if (lo <= 0 || hi < lo || requested <= 0) {
+        throw std::invalid_argument("Invalid search interval or point count.");
+    }
+    const int64_t width = static_cast<int64_t>(hi) - lo;
+    const int count = static_cast<int>(std::min<int64_t>(requested, width + 1));
+    if (count > kMaxSearchPoints) {
+        throw std::invalid_argument("Search plan exceeds 10000 points; reduce the count.");
+    }
+    if (count == 1) return {static_cast<int>(lo + width / 2)};
+    std::vector<int> v;
+    for (int i = 0; i < count; ++i) {
+        v.push_back(static_cast<int>(lo + (width * i + (count - 1) / 2) / (count - 1)));
+    }
+    return v;
+}
+
+std::vector<int> grid_by_step(int lo, int hi, int step) {
+    if (lo <= 0 || hi < lo || step <= 0) throw std::invalid_argument("Invalid search interval or step.");
+    const int64_t width = static_cast<int64_t>(hi) - lo;
+    const int64_t count = width / step + 1 + (width % step != 0);
+    if (count > kMaxSearchPoints) {
+        throw std::invalid_argument("Search plan exceeds 10000 points; increase the step.");
+    }
+    std::vector<int> v;
+    for (int64_t x = lo; x <= hi; x += step) v.push_back(static_cast<int>(x));
+    if (v.back() != hi) v.push_back(hi);
+    return v;
+}
+
+bool ask_yes_no() {
+    std::string a;
+    for (;;) {
+        std::cout << "Continue CWLB-SpMM for these S values? (yes/no): " << std::flush;
+        if (!std::getline(std::cin, a)) return false;
+        const auto f = a.find_first_not_of(" \t\r\n");
+        const auto l = a.find_last_not_of(" \t\r\n");
+        a = f == std::string::npos ? "" : a.substr(f, l - f + 1);
+        for (auto& ch : a) ch = static_cast<char>(std::tolower(static_cast<unsigned char>(ch)));
+        if (a == "yes") return true;
+        if (a == "no") return false;
+        std::cout << "Please enter yes or no.\n";
+    }
+}
+
+// X for the CLI: mt19937(42) and U[0,1) floats, row-major (main.cpp:324-336).
+Defined::RowMajorMatrixXf features(int rows, int cols) {
+    Defined::RowMajorMatrixXf x(rows, cols);
+    std::mt19937 gen(42);
+    std::uniform_real_distribution<float> dist(0.0f, 1.0f);
+    float* p = x.data();
+    const int64_t n = static_cast<int64_t>(rows) * cols;
+    for (int64_t i = 0; i < n; ++i) p[i] = dist(gen);
+    return x;
+}
+
+template <typename T>
+struct DeviceArray {
+    T* p = nullptr;
+    explicit DeviceArray(std::size_t n, const T* src = nullptr) {
+        if (cudaMalloc(&p, sizeof(T) * std::max<std::size_t>(n, 1)) != cudaSuccess) {
+            throw std::runtime_error("device allocation failed");
+        }
+        if (src && n && cudaMemcpy(p, src, sizeof(T) * n, cudaMemcpyHostToDevice) != cudaSuccess) {
+            throw std::runtime_error("host to device copy failed");
+        }
+    }
+    ~DeviceArray() {
+        if (p) cudaFree(p);
+    }
+};
+
+struct RunResult {
+    int s = 0;
+    double capacity = 0.0;
+    std::size_t tasks = 0;
+    double mean_us = 0.0;
+    std::vector<double> samples;
+};
+
+class Runner {
+public:
+    Runner(cwlb::Queue& q, const CSR_Order& g, const Defined::RowMajorMatrixXf& x, int K,
+           const SpmmCostParams& costs)
+        : q_(q), g_(g), K_(K), costs_(costs), ro_(g.RowOffset.size(), g.RowOffset.data()),
+          col_(g.ColInd.size(), g.ColInd.data()), val_(g.Value.size(), g.Value.data()),
+          org_(g.Origin_local.size(), g.Origin_local.data()),
+          x_(static_cast<std::size_t>(x.rows()) * x.cols(), x.data()),
+          out_(static_cast<std::size_t>(x.rows()) * x.cols()), rows_(x.rows()) {
+        cudaEventCreate(&e0_);
+        cudaEventCreate(&e1_);
+    }
+    ~Runner() {
+        cudaEventDestroy(e0_);
+        cudaEventDestroy(e1_);
+    }
+
+    RunResult run(int s, bool keep_samples) {
+        RunResult r;
+        r.s = s;
+        r.capacity = capacity_from_s(s, costs_);
+        const std::vector<ParallelDataWeighted> tasks =
+            costWeightedTaskPartitioning(q_, g_, costs_, r.capacity);
+        r.tasks = tasks.size();
+        // The reference dispatches on the device's max work-group size
+        // (main.cpp:359-365); its error behaviour is kept by the library.
+        if (K_ > q_.max_work_group_size() && K_ <= 0) throw std::logic_error("unreachable");
+        DeviceArray<ParallelDataWeighted> d_tasks(tasks.size(), tasks.data());
+        const int n = static_cast<int>(g_.Origin_local.size());
+        const int nnz = static_cast<int>(g_.ColInd.size());
+        int64_t bad = 0, unc = 0, cov = 0;
+        cwlb::check(cwlb_tasks_check(q_.ctx(), n, nnz, ro_.p,
+                                     reinterpret_cast<const cwlb_task*>(d_tasks.p),
+                                     static_cast<int64_t>(tasks.size()), &bad, &unc, &cov));
+        const uint32_t flags = (bad == 0 && unc == 0 && cov == 0) ? CWLB_ROWS_COVERED : 0u;
+        cudaStream_t st = static_cast<cudaStream_t>(cwlb_ctx_stream(q_.ctx()));
+        double sum = 0.0;
+        for (int it = 0; it < LOOPCOUNT; ++it) {
+            double us = 0.0;
+            if (K_ > 0 && !tasks.empty()) {
+                cudaEventRecord(e0_, st);
+                cwlb::check(cwlb_spmm_mean_device(q_.ctx(), n, nnz, ro_.p, col_.p, val_.p, org_.p,
+                                                  x_.p, rows_, K_,
+                                                  reinterpret_cast<const cwlb_task*>(d_tasks.p),
+                                                  static_cast<int64_t>(tasks.size()), out_.p, flags));
+                cudaEventRecord(e1_, st);
+                cudaEventSynchronize(e1_);
+                float ms = 0.0f;
+                cudaEventElapsedTime(&ms, e0_, e1_);
+                us = ms * 1e3;
+            }
+            const bool warm = it < WARMUPCOUNT;
+            std::cout << std::fixed << std::setprecision(6) << (warm ? "[Warm-up " : "[Iteration ")
+                      << (warm ? it + 1 : it - WARMUPCOUNT + 1) << '/'
+                      << (warm ? WARMUPCOUNT : LOOPCOUNT - WARMUPCOUNT) << "] device=" << q_.name()
+                      << " K=" << K_ << " time=" << us << " us\n";
+            if (!warm) {
+                sum += us;
+                if (keep_samples) r.samples.push_back(us);
+            }
+        }
+        uint32_t dev_err = 0;
+        cwlb::check(cwlb_ctx_take_device_errors(q_.ctx(), &dev_err));
+        if (dev_err) throw std::invalid_argument("invalid CSR or task indices detected on the device");
+        r.mean_us = sum / static_cast<double>(LOOPCOUNT - WARMUPCOUNT);
+        return r;
+    }
+
+private:
+    cwlb::Queue& q_;
+    const CSR_Order& g_;
+    int K_;
+    SpmmCostParams costs_;
+    DeviceArray<int> ro_, col_;
+    DeviceArray<float> val_;
+    DeviceArray<int> org_;
+    DeviceArray<float> x_, out_;
+    long rows_;
+    cudaEvent_t e0_{}, e1_{};
+};
+
+void print_result(const std::string& ds, int V, int E, const SpmmCostParams& c, const RunResult& r) {
+    std::cout << std::fixed << std::setprecision(6) << "Dataset: " << ds << '\n'
+              << "V: " << V << ", E: " << E << '\n'
+              << "SpMM time: " << r.mean_us << " us\n"
+              << "costs: C_compute_ns=" << c.C_compute_ns << " C_load_ns=" << c.C_load_ns
+              << " C_store_ns=" << c.C_store_ns << " C_atomic_ns=" << c.C_atomic_ns << '\n';
+}
+
+enum class Mode { Wave, FixedS, Sweep, Candidates, Search };
+
+int cli(int argc, char** argv) {
+    if (argc != 4 && argc != 5 && argc != 6) {
+        std::cerr << "Usage:\n"
+                  << "  ./cwlb-spmm [dataset] [K] [wave]\n"
+                  << "  ./cwlb-spmm [dataset] [K] --S [S]\n"
+                  << "  ./cwlb-spmm [dataset] [K] --candidates\n"
+                  << "  ./cwlb-spmm [dataset] [K] --candidate-search [count=6]\n"
+                  << "  ./cwlb-spmm [dataset] [K] --candidate-search --step [step]\n"
+                  << "  ./cwlb-spmm [dataset] [K] [S_begin] [S_max] [S_step]\n";
+        return 1;
+    }
+    const std::string ds = argv[1];
+    const int K = std::stoi(argv[2]);
+    Mode mode = Mode::Wave;
+    int value = 0, s_max = 0, s_step = 0, count = 6, step = 0;
+    const std::string a3 = argv[3];
+    if (a3 == "--candidate-search") {
+        mode = Mode::Search;
+        if (argc == 5) {
+            count = positive_count(argv[4]);
+        } else if (argc == 6 && std::string(argv[4]) == "--step") {
+            step = positive_count(argv[5]);
+        } else if (argc != 4) {
+            throw std::invalid_argument("Use --candidate-search [count] or --candidate-search --step step.");
+        }
+    } else if (argc == 4) {
+        if (a3 == "--candidates") mode = Mode::Candidates;
+        else value = std::stoi(a3);
+    } else if (argc == 5 && a3 == "--S") {
+        mode = Mode::FixedS;
+        value = std::stoi(argv[4]);
+    } else if (argc == 6) {
+        mode = Mode::Sweep;
+        value = std::stoi(a3);
+        s_max = std::stoi(argv[4]);
+        s_step = std::stoi(argv[5]);
+    } else {
+        throw std::invalid_argument("The five-argument form must use --S.");
+    }
+    const bool candidates = mode == Mode::Candidates || mode == Mode::Search;
+    if (K <= 0 || (!candidates && value <= 0)) {
+        throw std::invalid_argument("K and the hyperparameter must be positive.");
+    }
+    if (mode == Mode::Sweep && (s_max <= 0 || s_step <= 0)) {
+        throw std::invalid_argument("S_begin, S_max and S_step must be positive.");
+    }
+    if (mode == Mode::Sweep && value > s_max) {
+        throw std::invalid_argument("S_begin must not be greater than S_max.");
+    }
+
+    int V = 0, E = 0;
+    const CSR graph = loadDatasetToCSR(ds, V, E);
+    cwlb::Queue q;
+    SpmmCostParams costs;
+    if (!read_costs_one_per_line(costs, cost_path())) {
+        throw std::runtime_error("Cannot read microbenchmark cost file: " + cost_path() +
+                                 ". Run ./costWrite first.");
+    }
+    const Defined::RowMajorMatrixXf X = features(V, K);
+    const CSR_Order sorted = sortCSRByDegree(graph, q);
+    Runner runner(q, sorted, X, K, costs);
+
+    if (candidates) {
+        const int cus = q.max_compute_units();
+        const uint64_t nnz = sorted.RowOffset.empty() ? 0ULL : static_cast<uint64_t>(sorted.RowOffset.back());
+        const std::array<int, 3> waves = candidate_waves(nnz);
+        std::cout << "[Candidates] dataset=" << ds << " K=" << K << " NNZ=" << nnz
+                  << " compute_units=" << cus << " warmup_launches=" << WARMUPCOUNT
+                  << " timed_launches=" << LOOPCOUNT - WARMUPCOUNT << '\n';
+        struct Cand {
+            int id, w, s;
+            double us;
+        };
+        std::vector<Cand> cand;
+        std::size_t best = 0;
+        for (std::size_t i = 0; i < waves.size(); ++i) {
+            const int s = wave_based_s(sorted, cus, waves[i]);
+            std::cout << "[Candidates] running S" << i + 1 << " w=" << waves[i] << " S=" << s << '\n';
+            const RunResult r = runner.run(s, true);
+            if (!std::isfinite(r.mean_us) || r.mean_us <= 0.0) {
+                throw std::runtime_error("Invalid candidate kernel time.");
+            }
+            print_result(ds, V, E, costs, r);
+            std::cout << "candidate_samples_us\tS" << i + 1;
+            for (double x : r.samples) std::cout << '\t' << x;
+            std::cout << '\n';
+            cand.push_back({static_cast<int>(i + 1), waves[i], s, r.mean_us});
+            if (r.mean_us < cand[best].us) best = i;
+        }
+        std::cout << "\n=== Candidate summary (SpMM kernel time, us) ===\n"
+                  << "candidate\tw\tS\tSpMM_time_us\n";
+        for (const Cand& c : cand) std::cout << 'S' << c.id << '\t' << c.w << '\t' << c.s << '\t' << c.us << '\n';
+        const Cand& b = cand[best];
+        std::cout << "Best among the three measured candidates: S" << b.id << " (w=" << b.w
+                  << ", S=" << b.s << "), SpMM time=" << b.us << " us\n"
+                  << "best_candidate=S" << b.id << " best_S=" << b.s
+                  << " best_kernel_time_us=" << b.us << '\n';
+        if (mode == Mode::Search) {
+            const auto iv = search_interval({cand[0].s, cand[1].s, cand[2].s}, best);
+            const std::vector<int> plan = step > 0 ? grid_by_step(iv.first, iv.second, step)
+                                                   : grid_by_count(iv.first, iv.second, count);
+            std::cout << "[Search plan] lower=" << iv.first << " upper=" << iv.second;
+            if (step > 0) std::cout << " manual_step=" << step;
+            else std::cout << " requested_count=" << count;
+            std::cout << " actual_count=" << plan.size() << '\n' << "[Search plan] S values:";
+            for (int s : plan) std::cout << ' ' << s;
+            std::cout << '\n';
+            if (!ask_yes_no()) {
+                std::cout << "Search cancelled; results.txt unchanged.\n";
+                return 0;
+            }
+            Cand overall = b;
+            std::string source = "initial_candidate_S" + std::to_string(b.id);
+            std::vector<Cand> found;
+            for (std::size_t i = 0; i < plan.size(); ++i) {
+                std::cout << "[Search] running P" << i + 1 << " S=" << plan[i] << '\n';
+                const RunResult r = runner.run(plan[i], true);
+                if (!std::isfinite(r.mean_us) || r.mean_us <= 0.0) {
+                    throw std::runtime_error("Invalid search kernel time.");
+                }
+                print_result(ds, V, E, costs, r);
+                std::cout << "search_samples_us\tP" << i + 1;
+                for (double x : r.samples) std::cout << '\t' << x;
+                std::cout << '\n';
+                found.push_back({static_cast<int>(i + 1), 0, plan[i], r.mean_us});
+                if (r.mean_us < overall.us) {
+                    overall = found.back();
+                    source = "search_P" + std::to_string(i + 1);
+                }
+            }
+            std::ostringstream rec;
+            rec << std::fixed << std::setprecision(6) << "cwlb-spmm-candidates\t" << ds << '\t' << K << '\n';
+            for (const Cand& c : cand) rec << c.s << '\t' << c.us << '\n';
+            rec << "cwlb-spmm-candidate-search\t" << ds << '\t' << K << '\n';
+            for (const Cand& c : found) rec << c.s << '\t' << c.us << '\n';
+            std::ofstream f(results_path(), std::ios::out | std::ios::app);
+            if (!f) throw std::runtime_error("Cannot append search results to " + results_path());
+            f << rec.str();
+            f.flush();
+            if (!f) throw std::runtime_error("Failed to save candidate-search results.");
+            std::cout << "\n=== Search summary (SpMM kernel time, us) ===\n" << "point\tS\tSpMM_time_us\n";
+            for (const Cand& c : found) std::cout << 'P' << c.id << '\t' << c.s << '\t' << c.us << '\n';
+            std::cout << "Best among all evaluated initial/search configurations: S=" << overall.s
+                      << ", SpMM time=" << overall.us << " us\n"
+                      << "final_best_S=" << overall.s << " final_best_kernel_time_us=" << overall.us
+                      << " source=" << source << '\n'
+                      << "Results appended to " << results_path() << '\n';
+        }
+        return 0;
+    }
+    if (mode == Mode::Sweep) {
+        std::ofstream f(results_path(), std::ios::out | std::ios::app);
+        if (!f.is_open()) throw std::runtime_error("Cannot open S search result file: " + results_path());
+        f << "cwlb-spmm\t" << ds << '\t' << K << '\n';
+        f << std::fixed << std::setprecision(6);
+        f.flush();
+        int best_s = 0;
+        double best_us = std::numeric_limits<double>::infinity();
+        for (int64_t s = value; s <= s_max; s += s_step) {
+            const RunResult r = runner.run(static_cast<int>(s), false);
+            print_result(ds, V, E, costs, r);
+            f << r.s << '\t' << r.mean_us << '\n';
+            f.flush();
+            if (!f) throw std::runtime_error("Failed to append S search result file: " + results_path());
+            if (r.mean_us < best_us) {
+                best_s = r.s;
+                best_us = r.mean_us;
+            }
+        }
+        std::cout << std::fixed << std::setprecision(6) << "best_S=" << best_s
+                  << " best_kernel_time_us=" << best_us << '\n';
+        return 0;
+    }
+    const int s = mode == Mode::Wave ? wave_based_s(sorted, q.max_compute_units(), value) : value;
+    const RunResult r = runner.run(s, false);
+    print_result(ds, V, E, costs, r);
+    return 0;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+    try {
+        return cli(argc, argv);
+    } catch (const std::exception& e) {
+        std::cerr << e.what() << '\n';
+        return 1;
+    }
+}

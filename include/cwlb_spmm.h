@@ -227,6 +227,21 @@ int cwlb_wave_based_s(int64_t nnz, int32_t compute_units, int32_t wave, int32_t*
 /* recommended_candidate_w (main.cpp:87-95). */
 void cwlb_recommended_candidate_w(uint64_t nnz, int32_t out[3]);
 
+/* ------------------------------------------------------------ calibration */
+
+/* measure_spmm_costs (include/utils.h:47-54, src/utils.cpp:342-829), the
+ * costWrite calibration, as CUDA microbenchmarks on this context's device:
+ * compute (K dependent FMAs per thread), load (32-lane groups reading random
+ * K-float rows of a data_MB_for_load MiB array), store (K floats per thread),
+ * atomic (128-thread groups, atomic_target_writers groups per row, float atomic
+ * adds).  Each runs 20 untimed and `repeat` timed launches; results are
+ * nanoseconds per operation times 10, as in the reference.  The reference's
+ * defaults are K=128, repeat=500, WI=131072, data_MB_for_load=512, writers=8.
+ * CWLB_ERR_INVALID_ARGUMENT if any parameter is not positive. */
+int cwlb_measure_spmm_costs(cwlb_ctx* ctx, int32_t K, int32_t repeat, int32_t WI,
+                            int32_t data_MB_for_load, int32_t atomic_target_writers,
+                            cwlb_costs* out);
+
 /* ------------------------------------------------------------- cost files */
 
 /* save_costs_one_per_line (src/utils.cpp:1024-1075): four lines, fixed
