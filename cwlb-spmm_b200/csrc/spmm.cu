@@ -271,21 +271,43 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
     const int n_task_rows = tk.row_end - tk.row_start;
 
     if (G == 1 || n_task_rows != 1) {
-        // Each group takes its own rows (nnz order within a row preserved).
-        for (int r = tk.row_start + g; r < tk.row_end; r += G) {
+        // Rows go to teams of T groups.  With at least G rows, T = 1: each
+        // group takes its own rows and keeps nonzero order.  With fewer rows
+        // than groups, a team splits each row's nonzero chunks and reduces
+        // them with shuffles, so no group idles.
+        int T = 1;
+        if (G > 1) {
+            while (T * 2 * n_task_rows <= G) T *= 2;
+        }
+        const int teams = G / T;
+        const int team = g / T;
+        const int gt = g - team * T;
+        const int team_lanes = T * L;
+        const unsigned tmask = team_lanes == 32 ? 0xffffffffu
+                                                : (((1u << team_lanes) - 1u) << (team * team_lanes));
+        for (int r = tk.row_start + team; r < tk.row_end; r += teams) {
             RowFrag f;
             const int st = row_fragment(a, r, tk, f);
             if (st == 1) {
-                if (a.write_empty) write_zero_row<V>(a, f.orig, q, ok);
+                if (a.write_empty && gt == 0) write_zero_row<V>(a, f.orig, q, ok);
                 continue;
             }
             if (st != 0) continue;
             float4 acc[V];
 #pragma unroll
             for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            gather_chunks<L, V>(a, f.base + f.begin, f.base + f.end, L, gmask, lg, hq, ok, K4,
-                                acc);
-            write_row<V>(a, f, q, ok, acc);
+            gather_chunks<L, V>(a, f.base + f.begin + gt * L, f.base + f.end, team_lanes, gmask, lg,
+                                hq, ok, K4, acc);
+            for (int sh = L; sh < team_lanes; sh <<= 1) {
+#pragma unroll
+                for (int i = 0; i < V; ++i) {
+                    acc[i].x += __shfl_xor_sync(tmask, acc[i].x, sh);
+                    acc[i].y += __shfl_xor_sync(tmask, acc[i].y, sh);
+                    acc[i].z += __shfl_xor_sync(tmask, acc[i].z, sh);
+                    acc[i].w += __shfl_xor_sync(tmask, acc[i].w, sh);
+                }
+            }
+            if (gt == 0) write_row<V>(a, f, q, ok, acc);
         }
     } else {
         // One row: the G groups take interleaved chunks, then reduce by

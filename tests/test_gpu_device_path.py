@@ -83,3 +83,50 @@ def test_tasks_check_detects_gaps(ctx):
     r = ctx.tasks_check(4, 7, d_ro.data_ptr(), gap.data_ptr(), 2)
     assert r["uncovered_rows"] == 2 and r["nnz_coverage_errors"] == 3
     assert ctx.tasks_check(4, 7, d_ro.data_ptr(), bad.data_ptr(), 1)["bad_tasks"] == 1
+
+
+def test_x_far_larger_than_l2(ctx):
+    """X of 2.3M x 256 floats (2.4 GB, far larger than L2; most gathers miss
+    L2), checked against a float64 reference computed on the device by torch."""
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(17)
+    n, h_rows, K = 20000, 2_300_000, 256
+    deg = torch.randint(0, 60, (n,), generator=g, device=dev)
+    deg[::997] = 700  # a few long rows (split into fragments)
+    rowoff = torch.zeros(n + 1, dtype=torch.int64, device=dev)
+    rowoff[1:] = torch.cumsum(deg, 0)
+    nnz = int(rowoff[-1])
+    col = torch.randint(0, h_rows, (nnz,), generator=g, device=dev, dtype=torch.int32)
+    val = torch.randn(nnz, generator=g, device=dev)
+    X = torch.randn((h_rows, K), generator=g, device=dev)
+    ro32 = rowoff.to(torch.int32)
+    org = torch.empty(n, dtype=torch.int32, device=dev)
+    sro = torch.empty(n + 1, dtype=torch.int32, device=dev)
+    scol = torch.empty(nnz, dtype=torch.int32, device=dev)
+    sval = torch.empty(nnz, dtype=torch.float32, device=dev)
+    ctx.sort_by_degree_device(n, nnz, ro32.data_ptr(), col.data_ptr(), val.data_ptr(),
+                              org.data_ptr(), sro.data_ptr(), scol.data_ptr(), sval.data_ptr())
+    costs = cs.SpmmCostParams(0.0055, 0.018, 0.011, 0.5)
+    t_ptr, n_tasks = ctx.partition_device(n, sro.data_ptr(), costs, cs.capacity_from_s(64, costs))
+    out = torch.full((n, K), float("nan"), device=dev)
+    ctx.spmm_mean_device(n, nnz, sro.data_ptr(), scol.data_ptr(), sval.data_ptr(), org.data_ptr(),
+                         X.data_ptr(), h_rows, K, t_ptr, n_tasks, out.data_ptr(), 0)
+    torch.cuda.synchronize()
+    assert ctx.take_device_errors() == 0
+    rows = torch.repeat_interleave(torch.arange(n, device=dev), deg)
+    ref = torch.zeros((n, K), dtype=torch.float64, device=dev)
+    cond = torch.zeros((n, K), dtype=torch.float64, device=dev)
+    for c0 in range(0, nnz, 200_000):
+        c1 = min(nnz, c0 + 200_000)
+        prod = X[col[c0:c1].long()].double() * val[c0:c1].double()[:, None]
+        ref.index_add_(0, rows[c0:c1], prod)
+        cond.index_add_(0, rows[c0:c1], prod.abs())
+    d = deg.clamp_min(1).double()[:, None]
+    ref /= d
+    cond /= d
+    err = (out.double() - ref).abs()
+    scale = torch.maximum(ref.abs(), cond)
+    bad = err > 1e-5 * scale
+    bad &= ~((scale == 0) & (err == 0))
+    assert int(bad.sum()) == 0, float((err / scale.clamp_min(1e-30)).max())
