@@ -286,6 +286,19 @@ int cwlb_spmm_mean_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
     });
 }
 
+int cwlb_spmm_mean_reference_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
+                                    const int32_t* d_row_offset, const int32_t* d_col_ind,
+                                    const float* d_value, const float* d_H, int64_t h_rows,
+                                    int64_t K, float* d_out) {
+    return guarded([&] {
+        check_ctx(ctx);
+        require(n_rows >= 0 && nnz >= 0 && h_rows >= 0 && K >= 0, CWLB_ERR_INVALID_ARGUMENT,
+                "negative size");
+        cwlb::launch_spmm_mean_reference(ctx, n_rows, nnz, d_row_offset, d_col_ind, d_value, d_H,
+                                         h_rows, K, d_out);
+    });
+}
+
 int cwlb_tasks_check(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* d_row_offset,
                      const cwlb_task* d_tasks, int64_t n_tasks, int64_t* bad_tasks,
                      int64_t* uncovered_rows, int64_t* nnz_coverage_errors) {

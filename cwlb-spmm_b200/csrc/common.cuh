@@ -79,6 +79,10 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
                       const int32_t* col, const float* val, const int32_t* origin,
                       const float* H, int64_t h_rows, int64_t K, const cwlb_task* tasks,
                       int64_t n_tasks, float* out, uint32_t flags);
+// Float64 reference of the aggregation over an unsorted CSR (spmm.cu).
+void launch_spmm_mean_reference(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
+                                const int32_t* col, const float* val, const float* H,
+                                int64_t h_rows, int64_t K, float* out);
 void run_tasks_check(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                      const cwlb_task* tasks, int64_t n_tasks, int64_t* bad_tasks,
                      int64_t* uncovered_rows, int64_t* nnz_errors);

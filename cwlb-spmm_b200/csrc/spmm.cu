@@ -560,6 +560,71 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
 }
 
 // ---------------------------------------------------------------------------
+// Float64 reference aggregation (cwlb_spmm_mean_reference_device).
+//
+// Independent of the sort, the partitioner and the task kernels: one warp per
+// row of the caller's (unsorted) CSR, each lane owning columns lane, lane+32,
+// ... of a 256-column pass; the row's nonzeros are summed in order in double
+// and the mean is rounded once to float.
+
+namespace {
+
+constexpr int kRefCols = 8;  // columns per lane and pass (256 per warp)
+
+__global__ void __launch_bounds__(kThreads)
+spmm_mean_reference_kernel(const int32_t* __restrict__ rowoff, const int32_t* __restrict__ col,
+                           const float* __restrict__ val, const float* __restrict__ H,
+                           int64_t h_rows, int64_t K, int32_t n_rows, int32_t nnz,
+                           float* __restrict__ out, uint32_t* __restrict__ err) {
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= n_rows) return;
+    int32_t b = rowoff[row], e = rowoff[row + 1];
+    if (b < 0 || e < b || e > nnz) {
+        if (lane == 0) raise_err(err, CWLB_DEVERR_OFFSETS);
+        b = e = 0;
+    }
+    const int32_t deg = e - b;
+    float* orow = out + row * K;
+    for (int64_t k0 = 0; k0 < K; k0 += 32 * kRefCols) {
+        double acc[kRefCols];
+#pragma unroll
+        for (int i = 0; i < kRefCols; ++i) acc[i] = 0.0;
+        for (int32_t j = b; j < e; ++j) {
+            const int32_t c = col[j];
+            if (c < 0 || c >= h_rows) {
+                if (lane == 0) raise_err(err, CWLB_DEVERR_COL_RANGE);
+                continue;
+            }
+            const double v = static_cast<double>(val[j]);
+            const float* xrow = H + static_cast<int64_t>(c) * K;
+#pragma unroll
+            for (int i = 0; i < kRefCols; ++i) {
+                const int64_t k = k0 + lane + 32 * i;
+                if (k < K) acc[i] += v * static_cast<double>(xrow[k]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kRefCols; ++i) {
+            const int64_t k = k0 + lane + 32 * i;
+            if (k < K) orow[k] = deg > 0 ? static_cast<float>(acc[i] / static_cast<double>(deg)) : 0.0f;
+        }
+    }
+}
+
+}  // namespace
+
+void launch_spmm_mean_reference(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
+                                const int32_t* col, const float* val, const float* H,
+                                int64_t h_rows, int64_t K, float* out) {
+    if (n_rows <= 0 || K <= 0) return;
+    const unsigned blocks = static_cast<unsigned>(ceil_div(static_cast<int64_t>(n_rows), kWarpsPerCta));
+    spmm_mean_reference_kernel<<<blocks, kThreads, 0, ctx->stream>>>(
+        rowoff, col, val, H, h_rows, K, n_rows, nnz, out, ctx->d_error_flags);
+    CWLB_LAUNCH_CHECK("spmm_mean_reference_kernel");
+}
+
+// ---------------------------------------------------------------------------
 // Task-list validation (cwlb_tasks_check).
 
 namespace {

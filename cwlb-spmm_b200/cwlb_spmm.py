@@ -107,6 +107,9 @@ _sig("cwlb_recommended_candidate_w", [C.c_uint64, C.POINTER(_i32)], None)
 _sig("cwlb_save_costs", [C.POINTER(cwlb_costs), C.c_char_p, _i32, _i32])
 _sig("cwlb_measure_spmm_costs", [_vp, _i32, _i32, _i32, _i32, _i32, C.POINTER(cwlb_costs)])
 _sig("cwlb_read_costs", [C.POINTER(cwlb_costs), C.c_char_p])
+_sig("cwlb_spmm_mean_reference_device", [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _vp])
+_sig("cwlb_validate_result", [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _i64,
+                              _i64, C.c_float, C.POINTER(_i32)])
 
 
 def _check(rc):
@@ -339,6 +342,12 @@ class Context:
         _check(_lib.cwlb_spmm_mean_device(self._h, n_rows, nnz, d_rowoff, d_col, d_val, d_origin,
                                           d_H, h_rows, K, d_tasks, n_tasks, d_out, flags))
 
+    def spmm_mean_reference_device(self, n_rows, nnz, d_rowoff, d_col, d_val, d_H, h_rows, K,
+                                   d_out):
+        """Float64 reference aggregation over an unsorted CSR (original row order)."""
+        _check(_lib.cwlb_spmm_mean_reference_device(self._h, n_rows, nnz, d_rowoff, d_col, d_val,
+                                                    d_H, h_rows, K, d_out))
+
     def tasks_check(self, n_rows, nnz, d_rowoff, d_tasks, n_tasks):
         bad, unc, nz = _i64(), _i64(), _i64()
         _check(_lib.cwlb_tasks_check(self._h, n_rows, nnz, d_rowoff, d_tasks, n_tasks,
@@ -369,6 +378,60 @@ def recommended_candidate_w(nnz: int):
     out = (_i32 * 3)()
     _lib.cwlb_recommended_candidate_w(int(nnz), out)
     return [int(x) for x in out]
+
+
+def validate_custom_csr_result(result, reference, csr: CSR, dense_matrix,
+                               abs_tolerance: float = 1e-4) -> bool:
+    """validate_custom_csr_result (src/utils.cpp:1117-1265): element-wise check
+    of `result` against `reference`, printing the reference's report on the
+    process's stdout/stderr.  Host only."""
+    r = np.ascontiguousarray(result, np.float32)
+    f = np.ascontiguousarray(reference, np.float32)
+    d = np.ascontiguousarray(dense_matrix, np.float32)
+    r2, f2, d2 = (a if a.ndim == 2 else a.reshape(-1, 1) for a in (r, f, d))
+    passed = _i32()
+    _check(_lib.cwlb_validate_result(_p(r2), r2.shape[0], r2.shape[1], _p(f2), f2.shape[0],
+                                     f2.shape[1], _p(csr.RowOffset), len(csr.RowOffset),
+                                     _p(csr.ColInd), _p(csr.Value), _p(d2), d2.shape[0],
+                                     d2.shape[1], float(abs_tolerance), C.byref(passed)))
+    return passed.value != 0
+
+
+CSR_CACHE_MAGIC = b"CWLBCSR1"
+
+
+def read_csr_cache(text_path: str):
+    """Reads the binary cache the C++ loader writes beside a text CSR
+    ("<file>.csr.cwlbbin": 64-byte header, int32 RowOffset[V+1], int32
+    ColInd[E]; values 1.0f).  Returns a CSR, or None when the cache is
+    missing, stale (the text file's size or modification time changed) or
+    corrupt."""
+    import os
+    path = text_path + ".cwlbbin"
+    try:
+        st = os.stat(text_path)
+        with open(path, "rb") as f:
+            raw = f.read()
+    except OSError:
+        return None
+    if len(raw) < 64 or raw[:8] != CSR_CACHE_MAGIC:
+        return None
+    ver, hdr = np.frombuffer(raw, "<u4", 2, 8)
+    size, mtime, rows, nnz, checksum = (np.frombuffer(raw, "<u8", 1, 16)[0],
+                                        *np.frombuffer(raw, "<i8", 3, 24),
+                                        np.frombuffer(raw, "<u8", 1, 48)[0])
+    if (ver != 1 or hdr != 64 or size != st.st_size or mtime != st.st_mtime_ns or rows < 0 or
+            nnz < 0 or len(raw) != 64 + 4 * (rows + 1) + 4 * nnz):
+        return None
+    words = np.frombuffer(raw, "<u4", (len(raw) - 64) // 4, 64)
+    h = 1469598103934665603
+    for w in words.tolist():
+        h = ((h ^ w) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    if h != int(checksum):
+        return None
+    ro = words[:rows + 1].view("<i4")
+    col = words[rows + 1:].view("<i4")
+    return CSR(ro, col, np.ones(nnz, np.float32))
 
 
 def save_costs_one_per_line(costs: SpmmCostParams, filepath: str, append: bool = False,

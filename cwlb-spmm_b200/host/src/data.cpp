@@ -8,9 +8,15 @@
 // following digits, ignores what trails them, throws std::invalid_argument
 // without digits and std::out_of_range outside int) and the same checks and
 // messages, in the same order.
+#include <sys/stat.h>
+#include <unistd.h>
+
 #include <cctype>
+#include <climits>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -113,11 +119,156 @@ CSR loadTextCSRPath(const std::string& path, int& V, int& E) {
     return csr;
 }
 
-CSR loadDatasetToCSR(const std::string& datasetName, int& V, int& E) {
+namespace {
+
+std::string dataset_path(const std::string& datasetName) {
     if (datasetName.empty()) throw std::runtime_error("Dataset name is empty");
     const std::string name = ends_with(datasetName, ".csr") ? datasetName : datasetName + ".csr";
     const char* dir = std::getenv("CWLB_DATASET_DIR");
     std::string base = dir ? std::string(dir) : std::string(DATA_CSR_FILE_PATH);
     if (dir && !base.empty() && base.back() != '/') base += '/';
-    return loadTextCSRPath(base + name, V, E);
+    return base + name;
+}
+
+}  // namespace
+
+CSR loadDatasetToCSR(const std::string& datasetName, int& V, int& E) {
+    return loadTextCSRPath(dataset_path(datasetName), V, E);
+}
+
+// ---------------------------------------------------------------------------
+// Binary cache.
+
+namespace {
+
+constexpr char kCacheMagic[8] = {'C', 'W', 'L', 'B', 'C', 'S', 'R', '1'};
+constexpr uint32_t kCacheVersion = 1;
+
+struct CacheHeader {
+    char magic[8];
+    uint32_t version;
+    uint32_t header_bytes;
+    uint64_t source_size;
+    int64_t source_mtime_ns;
+    int64_t rows;
+    int64_t nnz;
+    uint64_t checksum;
+    uint64_t reserved;
+};
+static_assert(sizeof(CacheHeader) == 64, "cache header layout");
+
+bool source_stamp(const std::string& path, uint64_t& size, int64_t& mtime_ns) {
+    struct stat st {};
+    if (::stat(path.c_str(), &st) != 0) return false;
+    size = static_cast<uint64_t>(st.st_size);
+    mtime_ns = static_cast<int64_t>(st.st_mtim.tv_sec) * 1000000000LL + st.st_mtim.tv_nsec;
+    return true;
+}
+
+// FNV-1a over 32-bit words.
+uint64_t checksum_words(const int* p, std::size_t n, uint64_t h) {
+    for (std::size_t i = 0; i < n; ++i) {
+        h ^= static_cast<uint32_t>(p[i]);
+        h *= 1099511628211ULL;
+    }
+    return h;
+}
+
+uint64_t csr_checksum(const CSR& csr) {
+    const uint64_t h = checksum_words(csr.RowOffset.data(), csr.RowOffset.size(),
+                                      1469598103934665603ULL);
+    return checksum_words(csr.ColInd.data(), csr.ColInd.size(), h);
+}
+
+}  // namespace
+
+std::string csrCachePath(const std::string& text_path) { return text_path + ".cwlbbin"; }
+
+bool writeCSRCache(const CSR& csr, const std::string& text_path) {
+    CacheHeader h{};
+    std::memcpy(h.magic, kCacheMagic, sizeof(h.magic));
+    h.version = kCacheVersion;
+    h.header_bytes = sizeof(CacheHeader);
+    if (!source_stamp(text_path, h.source_size, h.source_mtime_ns)) return false;
+    if (csr.RowOffset.empty()) return false;
+    h.rows = static_cast<int64_t>(csr.RowOffset.size()) - 1;
+    h.nnz = static_cast<int64_t>(csr.ColInd.size());
+    h.checksum = csr_checksum(csr);
+    const std::string final_path = csrCachePath(text_path);
+    const std::string tmp = final_path + ".tmp" + std::to_string(static_cast<long>(::getpid()));
+    std::FILE* f = std::fopen(tmp.c_str(), "wb");
+    if (!f) return false;
+    bool ok = std::fwrite(&h, sizeof(h), 1, f) == 1 &&
+              std::fwrite(csr.RowOffset.data(), sizeof(int), csr.RowOffset.size(), f) ==
+                  csr.RowOffset.size() &&
+              (csr.ColInd.empty() ||
+               std::fwrite(csr.ColInd.data(), sizeof(int), csr.ColInd.size(), f) ==
+                   csr.ColInd.size());
+    ok = (std::fclose(f) == 0) && ok;
+    if (ok) ok = std::rename(tmp.c_str(), final_path.c_str()) == 0;
+    if (!ok) std::remove(tmp.c_str());
+    return ok;
+}
+
+bool readCSRCache(const std::string& text_path, CSR& csr, int& V, int& E) {
+    uint64_t size = 0;
+    int64_t mtime = 0;
+    if (!source_stamp(text_path, size, mtime)) return false;
+    std::FILE* f = std::fopen(csrCachePath(text_path).c_str(), "rb");
+    if (!f) return false;
+    CacheHeader h{};
+    CSR c;
+    bool ok = std::fread(&h, sizeof(h), 1, f) == 1 &&
+              std::memcmp(h.magic, kCacheMagic, sizeof(h.magic)) == 0 &&
+              h.version == kCacheVersion && h.header_bytes == sizeof(CacheHeader) &&
+              h.source_size == size && h.source_mtime_ns == mtime && h.rows >= 0 &&
+              h.rows < INT_MAX && h.nnz >= 0 && h.nnz <= INT_MAX;
+    if (ok) {
+        // The file must hold exactly the two arrays after the header.
+        const long want = static_cast<long>(sizeof(CacheHeader)) + 4L * (h.rows + 1) + 4L * h.nnz;
+        ok = std::fseek(f, 0, SEEK_END) == 0 && std::ftell(f) == want &&
+             std::fseek(f, static_cast<long>(sizeof(CacheHeader)), SEEK_SET) == 0;
+    }
+    if (ok) {
+        c.RowOffset.resize(static_cast<std::size_t>(h.rows) + 1);
+        c.ColInd.resize(static_cast<std::size_t>(h.nnz));
+        ok = std::fread(c.RowOffset.data(), sizeof(int), c.RowOffset.size(), f) ==
+                 c.RowOffset.size() &&
+             (c.ColInd.empty() ||
+              std::fread(c.ColInd.data(), sizeof(int), c.ColInd.size(), f) == c.ColInd.size());
+    }
+    std::fclose(f);
+    if (!ok || csr_checksum(c) != h.checksum || c.RowOffset.front() != 0 ||
+        c.RowOffset.back() != h.nnz) {
+        return false;
+    }
+    // The invariants the text loader checked before the cache was written.
+    for (std::size_t i = 1; i < c.RowOffset.size(); ++i) {
+        if (c.RowOffset[i] < c.RowOffset[i - 1]) return false;
+    }
+    for (int col : c.ColInd) {
+        if (col < 0) return false;
+    }
+    c.Value.assign(c.ColInd.size(), 1.0f);
+    V = static_cast<int>(h.rows);
+    E = static_cast<int>(h.nnz);
+    csr = std::move(c);
+    return true;
+}
+
+CSR loadTextCSRPathCached(const std::string& path, int& V, int& E, CsrCacheStatus* status) {
+    CSR csr;
+    if (readCSRCache(path, csr, V, E)) {
+        if (status) *status = CsrCacheStatus::Hit;
+        return csr;
+    }
+    csr = loadTextCSRPath(path, V, E);
+    const bool written = writeCSRCache(csr, path);
+    if (status) *status = written ? CsrCacheStatus::Written : CsrCacheStatus::NotWritten;
+    return csr;
+}
+
+CSR loadDatasetToCSRCached(const std::string& datasetName, int& V, int& E,
+                           CsrCacheStatus* status) {
+    return loadTextCSRPathCached(dataset_path(datasetName), V, E, status);
 }

@@ -137,87 +137,13 @@ std::vector<std::pair<int, float>> get_csr_row_elements(const CSR& csr, int row)
 bool validate_custom_csr_result(const Defined::RowMajorMatrixXf& result,
                                 const Defined::RowMajorMatrixXf& reference, const CSR& csr,
                                 const Defined::RowMajorMatrixXf& dense, float abs_tolerance) {
-    try {
-        if (abs_tolerance < 0.0f || !std::isfinite(abs_tolerance)) {
-            throw std::invalid_argument("Validation tolerance must be finite and non-negative.");
-        }
-        if (result.rows() != reference.rows() || result.cols() != reference.cols()) {
-            std::cerr << "Validation failed: result matrix shape is (" << result.rows() << ", "
-                      << result.cols() << "), but reference matrix shape is ("
-                      << reference.rows() << ", " << reference.cols() << ").\n";
-            return false;
-        }
-        if (csr.RowOffset.size() != static_cast<std::size_t>(reference.rows()) + 1) {
-            std::cerr << "Validation failed: CSR row count does not match the reference matrix.\n";
-            return false;
-        }
-        if (dense.rows() <= 0 || dense.cols() != reference.cols()) {
-            std::cerr << "Validation failed: input dense matrix shape is incompatible with the "
-                         "reference result.\n";
-            return false;
-        }
-        std::vector<ErrorElement> errors;
-        for (long r = 0; r < reference.rows() && errors.size() < 10; ++r) {
-            for (long c = 0; c < reference.cols() && errors.size() < 10; ++c) {
-                const float got = result(r, c), want = reference(r, c);
-                bool bad;
-                float err;
-                if (std::isnan(got) || std::isnan(want)) {
-                    bad = !(std::isnan(got) && std::isnan(want));
-                    err = bad ? std::numeric_limits<float>::infinity() : 0.0f;
-                } else if (std::isinf(got) || std::isinf(want)) {
-                    bad = got != want;
-                    err = bad ? std::numeric_limits<float>::infinity() : 0.0f;
-                } else {
-                    err = std::abs(got - want);
-                    bad = err > abs_tolerance;
-                }
-                if (!bad) continue;
-                ErrorElement e;
-                e.result_row = static_cast<int>(r);
-                e.result_col = static_cast<int>(c);
-                e.sycl_value = got;
-                e.reference_value = want;
-                e.absolute_error = err;
-                e.csr_row_elements = get_csr_row_elements(csr, static_cast<int>(r));
-                for (long d = 0; d < dense.rows(); ++d) e.dense_col_elements.push_back(dense(d, c));
-                errors.push_back(std::move(e));
-            }
-        }
-        if (errors.empty()) {
-            std::cout << "\033[1;32mValidation passed: all elements satisfy the comparison "
-                         "criteria.\033[0m\n";
-            return true;
-        }
-        std::cout << "\033[1;31mValidation failed: showing " << errors.size()
-                  << " mismatched elements (up to the first 10).\033[0m\n";
-        for (std::size_t i = 0; i < errors.size(); ++i) {
-            const ErrorElement& e = errors[i];
-            std::cout << "\nStored entries in CSR row " << e.result_row << ":\n"
-                      << "RowOffset[" << e.result_row << "]: " << csr.RowOffset[e.result_row] << '\n'
-                      << "RowOffset[" << e.result_row + 1 << "]: " << csr.RowOffset[e.result_row + 1]
-                      << '\n'
-                      << "Format: [ColInd] -> Value\n";
-            for (const auto& el : e.csr_row_elements) {
-                std::cout << "  [" << el.first << "] -> " << el.second << '\n';
-            }
-            std::cout << "\nDense matrix column " << e.result_col << " (up to the first 5 rows):\n";
-            const int shown = std::min<int>(5, static_cast<int>(e.dense_col_elements.size()));
-            for (int d = 0; d < shown; ++d) {
-                std::cout << "  Row " << d << ": " << e.dense_col_elements[d] << '\n';
-            }
-            std::cout << "\n\033[1;34mMismatch #" << i + 1 << ":\033[0m\n"
-                      << "Result matrix position: (" << e.result_row << ", " << e.result_col << ")\n"
-                      << std::fixed << std::setprecision(6) << "SYCL result:     " << e.sycl_value
-                      << '\n'
-                      << "Reference value: " << e.reference_value << '\n'
-                      << "Absolute error:  " << e.absolute_error << '\n';
-        }
-        return false;
-    } catch (const std::exception& e) {
-        std::cerr << "Validation error: " << e.what() << '\n';
-        return false;
-    }
+    int32_t passed = 0;
+    cwlb::check(cwlb_validate_result(result.data(), result.rows(), result.cols(), reference.data(),
+                                     reference.rows(), reference.cols(), csr.RowOffset.data(),
+                                     static_cast<int64_t>(csr.RowOffset.size()),
+                                     csr.ColInd.data(), csr.Value.data(), dense.data(),
+                                     dense.rows(), dense.cols(), abs_tolerance, &passed));
+    return passed != 0;
 }
 
 double capacity_from_s(int s, const SpmmCostParams& costs) {

@@ -10,6 +10,13 @@
 // Paths default to the reference's (../resources/...), overridable with
 // CWLB_DATASET_DIR, CWLB_COSTFILE and CWLB_RESULTS; CWLB_DEVICE picks the GPU.
 //
+// Extensions: CWLB_CSR_CACHE=1 loads the dataset through the binary cache
+// beside the text file (data.h), and a trailing --verify checks every run's output with
+// validate_custom_csr_result (absolute tolerance 1e-4) against a float64
+// aggregation of the UNSORTED CSR computed on the device
+// (cwlb_spmm_mean_reference_device), and exits with status 1 on a mismatch.
+// Without it, output and exit status are the reference's.
+//
 // Each S run partitions on the GPU, uploads the reordered CSR, X and the tasks
 // once, and times LOOPCOUNT aggregation launches with CUDA events (the first
 // WARMUPCOUNT are warm-up), reporting the mean of the timed ones in
@@ -166,8 +173,9 @@ struct RunResult {
 class Runner {
 public:
     Runner(cwlb::Queue& q, const CSR_Order& g, const Defined::RowMajorMatrixXf& x, int K,
-           const SpmmCostParams& costs)
-        : q_(q), g_(g), K_(K), costs_(costs), ro_(g.RowOffset.size(), g.RowOffset.data()),
+           const SpmmCostParams& costs, const CSR* verify_against = nullptr)
+        : q_(q), g_(g), K_(K), costs_(costs), x_host_(x), verify_(verify_against),
+          ro_(g.RowOffset.size(), g.RowOffset.data()),
           col_(g.ColInd.size(), g.ColInd.data()), val_(g.Value.size(), g.Value.data()),
           org_(g.Origin_local.size(), g.Origin_local.data()),
           x_(static_cast<std::size_t>(x.rows()) * x.cols(), x.data()),
@@ -228,14 +236,52 @@ public:
         cwlb::check(cwlb_ctx_take_device_errors(q_.ctx(), &dev_err));
         if (dev_err) throw std::invalid_argument("invalid CSR or task indices detected on the device");
         r.mean_us = sum / static_cast<double>(LOOPCOUNT - WARMUPCOUNT);
+        if (verify_) verify(s);
         return r;
     }
 
 private:
+    // Compares the last launch's output with the float64 device aggregation
+    // of the unsorted CSR (computed once).
+    void verify(int s) {
+        const std::size_t n = static_cast<std::size_t>(rows_) * static_cast<std::size_t>(K_);
+        if (reference_.rows() != rows_ || reference_.cols() != K_) {
+            const CSR& c = *verify_;
+            DeviceArray<int> ro(c.RowOffset.size(), c.RowOffset.data());
+            DeviceArray<int> col(c.ColInd.size(), c.ColInd.data());
+            DeviceArray<float> val(c.Value.size(), c.Value.data());
+            DeviceArray<float> ref(n);
+            cwlb::check(cwlb_spmm_mean_reference_device(
+                q_.ctx(), static_cast<int32_t>(c.RowOffset.size()) - 1,
+                static_cast<int32_t>(c.ColInd.size()), ro.p, col.p, val.p, x_.p, rows_, K_, ref.p));
+            q_.wait();
+            uint32_t dev_err = 0;
+            cwlb::check(cwlb_ctx_take_device_errors(q_.ctx(), &dev_err));
+            if (dev_err) throw std::invalid_argument("invalid CSR indices detected on the device");
+            reference_ = Defined::RowMajorMatrixXf(rows_, K_);
+            if (n && cudaMemcpy(reference_.data(), ref.p, sizeof(float) * n, cudaMemcpyDeviceToHost) !=
+                         cudaSuccess) {
+                throw std::runtime_error("device to host copy failed");
+            }
+        }
+        Defined::RowMajorMatrixXf result(rows_, K_);
+        if (n && cudaMemcpy(result.data(), out_.p, sizeof(float) * n, cudaMemcpyDeviceToHost) !=
+                     cudaSuccess) {
+            throw std::runtime_error("device to host copy failed");
+        }
+        std::cout << "[Verify] S=" << s << ' ';
+        if (!validate_custom_csr_result(result, reference_, *verify_, x_host_, 1e-4f)) {
+            throw std::runtime_error("Verification failed for S=" + std::to_string(s) + ".");
+        }
+    }
+
     cwlb::Queue& q_;
     const CSR_Order& g_;
     int K_;
     SpmmCostParams costs_;
+    const Defined::RowMajorMatrixXf& x_host_;
+    const CSR* verify_;
+    Defined::RowMajorMatrixXf reference_;
     DeviceArray<int> ro_, col_;
     DeviceArray<float> val_;
     DeviceArray<int> org_;
@@ -255,6 +301,8 @@ void print_result(const std::string& ds, int V, int E, const SpmmCostParams& c, 
 enum class Mode { Wave, FixedS, Sweep, Candidates, Search };
 
 int cli(int argc, char** argv) {
+    const bool verify = argc > 1 && std::string(argv[argc - 1]) == "--verify";
+    if (verify) --argc;
     if (argc != 4 && argc != 5 && argc != 6) {
         std::cerr << "Usage:\n"
                   << "  ./cwlb-spmm [dataset] [K] [wave]\n"
@@ -305,7 +353,9 @@ int cli(int argc, char** argv) {
     }
 
     int V = 0, E = 0;
-    const CSR graph = loadDatasetToCSR(ds, V, E);
+    const char* use_cache = std::getenv("CWLB_CSR_CACHE");
+    const CSR graph = (use_cache && std::string(use_cache) == "1") ? loadDatasetToCSRCached(ds, V, E)
+                                                                   : loadDatasetToCSR(ds, V, E);
     cwlb::Queue q;
     SpmmCostParams costs;
     if (!read_costs_one_per_line(costs, cost_path())) {
@@ -314,7 +364,7 @@ int cli(int argc, char** argv) {
     }
     const Defined::RowMajorMatrixXf X = features(V, K);
     const CSR_Order sorted = sortCSRByDegree(graph, q);
-    Runner runner(q, sorted, X, K, costs);
+    Runner runner(q, sorted, X, K, costs, verify ? &graph : nullptr);
 
     if (candidates) {
         const int cus = q.max_compute_units();

@@ -242,6 +242,38 @@ int cwlb_measure_spmm_costs(cwlb_ctx* ctx, int32_t K, int32_t repeat, int32_t WI
                             int32_t data_MB_for_load, int32_t atomic_target_writers,
                             cwlb_costs* out);
 
+/* ------------------------------------------------------------- validation */
+
+/* Float64 reference of the mean aggregation over an UNSORTED CSR (the
+ * caller's original row order): d_out[r, k] = (float)((1/deg_r) *
+ * sum_j value_j * H[col_j, k]) with the row's nonzeros summed in order in
+ * double, one warp per row; empty rows give 0.  It shares nothing with the
+ * sort, the partitioner or the task kernels, so it checks the whole path.
+ * No counterpart in the reference, whose validate_custom_csr_result compares
+ * against a result the caller supplies (src/utils.cpp:1117-1265); the
+ * cwlb-spmm CLI's --verify uses this to produce that result on the device.
+ * Asynchronous on the context's stream; bad indices raise device error flags
+ * as the aggregation kernels do. */
+int cwlb_spmm_mean_reference_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
+                                    const int32_t* d_row_offset, const int32_t* d_col_ind,
+                                    const float* d_value, const float* d_H, int64_t h_rows,
+                                    int64_t K, float* d_out);
+
+/* validate_custom_csr_result (src/utils.cpp:1117-1265) on host arrays:
+ * compares `result` with `reference` element by element (NaN matches only
+ * NaN, an infinity only the same infinity, finite values within
+ * abs_tolerance) and prints, like the reference, a pass line or up to 10
+ * mismatches with the CSR row (row_offset has row_offset_len entries) and the
+ * first 5 entries of the dense matrix's column; shape problems and a bad
+ * tolerance are reported on stderr.  *passed receives 1 or 0.  Host code: no
+ * context or device is needed. */
+int cwlb_validate_result(const float* result, int64_t result_rows, int64_t result_cols,
+                         const float* reference, int64_t reference_rows, int64_t reference_cols,
+                         const int32_t* row_offset, int64_t row_offset_len,
+                         const int32_t* col_ind, const float* value, const float* dense,
+                         int64_t dense_rows, int64_t dense_cols, float abs_tolerance,
+                         int32_t* passed);
+
 /* ------------------------------------------------------------- cost files */
 
 /* save_costs_one_per_line (src/utils.cpp:1024-1075): four lines, fixed

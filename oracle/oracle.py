@@ -166,6 +166,9 @@ class Reference:
         lib.cwlbref_load_csr_fetch.argtypes = [_i32p, _i32p, _f32p]
         lib.cwlbref_validate.argtypes = [_f32p, _f32p, C.c_long, C.c_long, C.c_int, C.c_int,
                                          _i32p, _i32p, _f32p, _f32p, C.c_long, C.c_float]
+        _v, _l = C.c_void_p, C.c_long
+        lib.cwlbref_validate_shapes.argtypes = [_v, _l, _l, _v, _l, _l, _v, _l, _v, _l, _v, _v, _l,
+                                                _l, C.c_float]
         lib.cwlbref_measure_costs.argtypes = [C.c_int] * 5 + [_f64p]
         lib.cwlbref_main.argtypes = [C.c_int, C.POINTER(C.c_char_p)]
         lib.cwlbref_costwrite_main.argtypes = [C.c_int, C.POINTER(C.c_char_p)]
@@ -283,6 +286,17 @@ class Reference:
                                               result.shape[1], len(rowoff) - 1, len(col),
                                               _c_i32(rowoff), _c_i32(col), _c_f32(val), dense,
                                               dense.shape[0], abs_tol))
+
+    def validate_shapes(self, result, reference, rowoff, col, val, dense, abs_tol=1e-4):
+        """validate_custom_csr_result with each matrix's own shape (2-D arrays)."""
+        r, f, d = (np.ascontiguousarray(a, np.float32) for a in (result, reference, dense))
+        ro, c = np.ascontiguousarray(rowoff, np.int32), np.ascontiguousarray(col, np.int32)
+        v = np.ascontiguousarray(val, np.float32)
+        p = lambda a: a.ctypes.data if a.size else None
+        return bool(self.lib.cwlbref_validate_shapes(p(r), r.shape[0], r.shape[1], p(f),
+                                                     f.shape[0], f.shape[1], p(ro), len(ro), p(c),
+                                                     len(c), p(v), p(d), d.shape[0], d.shape[1],
+                                                     float(abs_tol)))
 
     def main(self, argv):
         arr = (C.c_char_p * len(argv))(*[a.encode() for a in argv])

@@ -247,6 +247,24 @@ int cwlbref_validate(const float* result, const float* reference, long rows, lon
     return validate_custom_csr_result(r, ref, csr, d, abs_tol) ? 1 : 0;
 }
 
+// src/utils.cpp:1117-1265 with independent shapes for the result, the
+// reference and the dense matrix, and the CSR given by its RowOffset length
+// (the shape checks need all of them).  Returns 1 when the comparison passes.
+int cwlbref_validate_shapes(const float* result, long rr, long rc, const float* reference,
+                            long fr, long fc, const int* rowoff, long rowoff_len, const int* col,
+                            long nnz, const float* val, const float* dense, long dr, long dc,
+                            float abs_tol) {
+    Defined::RowMajorMatrixXf r(rr, rc), ref(fr, fc), d(dr, dc);
+    if (rr * rc) std::memcpy(r.data(), result, sizeof(float) * rr * rc);
+    if (fr * fc) std::memcpy(ref.data(), reference, sizeof(float) * fr * fc);
+    if (dr * dc) std::memcpy(d.data(), dense, sizeof(float) * dr * dc);
+    CSR csr;
+    csr.RowOffset.assign(rowoff, rowoff + rowoff_len);
+    csr.ColInd.assign(col, col + nnz);
+    csr.Value.assign(val, val + nnz);
+    return validate_custom_csr_result(r, ref, csr, d, abs_tol) ? 1 : 0;
+}
+
 // weightCost.cpp / src/utils.cpp:342-829 run on the emulated device.
 int cwlbref_measure_costs(int K, int repeat, int WI, int load_mb, int writers, double* out) {
     return guarded([&] {

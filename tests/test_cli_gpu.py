@@ -133,6 +133,46 @@ def test_cli_large_k_runs(workdir):
     assert re.search(r"SpMM time: [0-9.]+ us", out)
 
 
+@pytest.mark.parametrize("argv", [["g", "16", "--S", "8"], ["g", "13", "4"], ["g", "1100", "--S", "16"],
+                                  ["g", "8", "--candidates"]])
+def test_cli_verify_checks_every_run(workdir, argv):
+    rc, out, err = run([CWLB, *argv, "--verify"], workdir / "build")
+    assert rc == 0, err
+    runs = len(re.findall(r"SpMM time: ", out))
+    assert runs >= 1
+    assert out.count("Validation passed: all elements satisfy the comparison criteria.") == runs
+    assert len(re.findall(r"\[Verify\] S=\d+ ", out)) == runs
+    # Without --verify the output carries no verification lines.
+    rc, out2, err = run([CWLB, *argv], workdir / "build")
+    assert rc == 0 and "[Verify]" not in out2
+
+
+def test_cli_verify_with_out_of_range_column_fails(workdir):
+    # A column beyond the row count is caught by the aggregation's own checks
+    # (exit status 1) before any verification.  Mismatch reports themselves
+    # are checked against the reference on CPU (test_validate_cpu.py).
+    (workdir / "resources" / "datasets" / "bad.csr").write_text("0,1,2\n0,9\n")
+    rc, out, err = run([CWLB, "bad", "16", "--S", "4", "--verify"], workdir / "build")
+    assert rc == 1 and "[Verify]" not in out
+
+
+def test_cli_csr_cache(workdir):
+    # CWLB_CSR_CACHE=1: the first run writes the binary cache beside the text
+    # file, the second reads it; output grammar and the graph are unchanged.
+    env = _env()
+    env["CWLB_CSR_CACHE"] = "1"
+    argv = [CWLB, "g", "16", "--S", "8", "--verify"]
+    outs = []
+    for _ in range(2):
+        p = subprocess.run(argv, cwd=workdir / "build", capture_output=True, text=True, env=env,
+                           timeout=900)
+        assert p.returncode == 0, p.stderr
+        outs.append(p.stdout)
+    assert (workdir / "resources" / "datasets" / "g.csr.cwlbbin").exists()
+    assert template(outs[0]) == template(outs[1])
+    assert "V: 512, E: " in outs[1] and "Validation passed" in outs[1]
+
+
 def test_costwrite_writes_cost_file(workdir):
     rc, out, err = run([COSTWRITE, "32", "5", "8192", "16", "4"], workdir / "build")
     assert rc == 0, err

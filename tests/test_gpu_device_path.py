@@ -130,3 +130,44 @@ def test_x_far_larger_than_l2(ctx):
     bad = err > 1e-5 * scale
     bad &= ~((scale == 0) & (err == 0))
     assert int(bad.sum()) == 0, float((err / scale.clamp_min(1e-30)).max())
+
+
+@pytest.mark.parametrize("K", [1, 7, 32, 300])
+def test_reference_kernel_matches_oracle_f64(ctx, oracle, K):
+    """cwlb_spmm_mean_reference_device (unsorted CSR, float64 sums, one
+    rounding) against the oracle's exact mean: within one float rounding."""
+    rng = np.random.default_rng(40 + K)
+    from helpers import random_csr
+    rowoff, col, val = random_csr(rng, 3000, 40, n_cols=2500, hubs=3, hub_factor=200)
+    n, nnz = len(rowoff) - 1, len(col)
+    X = rng.standard_normal((2500, K)).astype(np.float32)
+    dev = torch.device("cuda:0")
+    d = [torch.from_numpy(a).to(dev) for a in (rowoff, col, val, X)]
+    out = torch.full((n, K), float("nan"), device=dev)
+    ctx.spmm_mean_reference_device(n, nnz, d[0].data_ptr(), d[1].data_ptr(), d[2].data_ptr(),
+                                   d[3].data_ptr(), 2500, K, out.data_ptr())
+    torch.cuda.synchronize()
+    assert ctx.take_device_errors() == 0
+    ref, cond = oracle.spmm_mean_f64(rowoff, col, val, np.arange(n, dtype=np.int32), X)
+    got = out.cpu().numpy().astype(np.float64)
+    # Rounded once from a double sum: error <= half an ulp of the result plus
+    # the two double sums' own errors (below 1e-11 of the condition scale for
+    # rows of up to 8000 nonzeros).
+    scale = np.maximum(np.abs(ref), cond)
+    assert np.all(np.abs(got - ref) <= np.abs(ref) * 2.0 ** -24 + 1e-11 * scale)
+    assert np.all(got[np.diff(rowoff) == 0] == 0.0)
+
+
+def test_reference_kernel_flags_bad_columns(ctx):
+    dev = torch.device("cuda:0")
+    ro = torch.tensor([0, 2, 3], dtype=torch.int32, device=dev)
+    col = torch.tensor([0, 5, 1], dtype=torch.int32, device=dev)  # 5 >= h_rows
+    val = torch.ones(3, device=dev)
+    X = torch.arange(8, dtype=torch.float32, device=dev).reshape(2, 4)
+    out = torch.empty((2, 4), device=dev)
+    ctx.spmm_mean_reference_device(2, 3, ro.data_ptr(), col.data_ptr(), val.data_ptr(),
+                                   X.data_ptr(), 2, 4, out.data_ptr())
+    torch.cuda.synchronize()
+    assert ctx.take_device_errors() == cs.DEVERR_COL_RANGE
+    # The bad entry is skipped; the mean still divides by the stored degree.
+    assert torch.equal(out.cpu(), torch.tensor([[0., 0.5, 1., 1.5], [4., 5., 6., 7.]]))
