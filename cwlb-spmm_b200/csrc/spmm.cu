@@ -129,15 +129,20 @@ __device__ __forceinline__ bool load_task(const SpmmArgs& a, int64_t t, cwlb_tas
 // (an out-of-range column becomes (0, 0.0f) and raises CWLB_DEVERR_COL_RANGE);
 // the pairs are then broadcast inside the group with __shfl_sync, so every
 // nonzero costs two shuffles, one wide address multiply-add, V 16-byte loads
-// and 4V FMAs.  Loads are unconditional: lanes past the end of a partial
-// chunk hold column 0 (valid) and skip only the FMA; padding lanes of a
-// partial K tile read a valid column and never write.
+// and 4V FMAs.  Loads of a full chunk are unconditional; in a partial chunk
+// the slots past its end hold column 0 (valid) and skip the FMA (and, for
+// narrow shapes, the load); padding lanes of a partial K tile read a valid
+// column and never write.
 
 template <int L, int V>
 struct VecCfg {
     static constexpr int G = 32 / L;
     static constexpr int U0 = V == 1 ? 8 : (V == 2 ? 4 : 2);
     static constexpr int U = U0 < L ? U0 : L;
+    // Rows of at most 64 floats (short-row graphs): partial chunks skip the
+    // X loads of their unused slots.  Wider shapes load unconditionally: the
+    // predicates cost them registers and an occupancy step.
+    static constexpr bool kSkipUnused = L * V <= 16;
 };
 
 // Accumulate the nonzeros of chunks starting at `start`, `start + step`, ...
@@ -200,8 +205,15 @@ __device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, 
 #pragma unroll
                 for (int t = 0; t < U; ++t) {
 #pragma unroll
-                    for (int i = 0; i < V; ++i)
-                        x[t][i] = __ldg(hq[i] + static_cast<size_t>(cu[t]) * K4);
+                    for (int i = 0; i < V; ++i) {
+                        if (VecCfg<L, V>::kSkipUnused) {
+                            x[t][i] = (u0 + t < cnt)
+                                          ? __ldg(hq[i] + static_cast<size_t>(cu[t]) * K4)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+                        } else {
+                            x[t][i] = __ldg(hq[i] + static_cast<size_t>(cu[t]) * K4);
+                        }
+                    }
                 }
 #pragma unroll
                 for (int t = 0; t < U; ++t) {
@@ -474,9 +486,19 @@ void launch_vec_v(int V, const SpmmArgs& a, cudaStream_t s) {
     }
 }
 
-// Picks (L, V) for K4 float4 columns: the least padding, then the widest
-// group (fewest groups per warp).
+// Picks (L, V) for K4 float4 columns.  Two widths use shapes measured
+// fastest on B200: K = 32 -> <4,2> and K = 128 -> <16,2> (two float4 per lane
+// halve the shuffles per nonzero and double the rows in flight; 10% and 2%
+// faster than <8,1> and <32,1> on configurations 4 and 2).  K = 64 keeps
+// <16,1>: <8,2> was 5% slower on configuration 5, where more rows in flight
+// cost L1 hits on its hub rows.  Other widths: the least padding, then the
+// widest group (fewest groups per warp).
 void pick_vec_shape(int64_t K4, int& L, int& V) {
+    if (K4 == 8 || K4 == 32) {
+        L = static_cast<int>(K4 / 2);
+        V = 2;
+        return;
+    }
     int64_t best_waste = -1;
     for (int l = 32; l >= 1; l >>= 1) {
         for (int v = 1; v <= 4; ++v) {
