@@ -12,7 +12,9 @@ GFLOP/s (2 * nnz * K per step) with HBM GB/s against the measured roofline.
 Multi-GPU (torchrun, one rank per GPU): every rank builds the same graph,
 takes a contiguous, cost-balanced block of ORIGINAL rows (X replicated), sorts
 and partitions it on its GPU, and aggregates it; no collective on the data
-path.  Total work is fixed as N grows ("strong" scaling).
+path.  Total work is fixed as N grows ("strong" scaling).  With --x-sharded,
+X starts row-sharded (each rank holds the rows it owns, as a prior layer's
+output leaves it) and every timed step all-gathers it over NCCL first.
 
 Outside the timed region: graph synthesis (torch, seeded), degree sort,
 partition (both on the GPU), the S choice (the reference's --candidates
@@ -63,6 +65,9 @@ def parse_args():
                     help="shrink the configuration (profiling captures only; not a bench line)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--x-sharded", action="store_true",
+                    help="N > 1: X arrives row-sharded (as a prior layer leaves it); every "
+                         "step all-gathers it over NCCL before the aggregation")
     return ap.parse_args()
 
 
@@ -204,11 +209,14 @@ def build_workload(cfg_id, device, world, rank, costs, scale_down=1):
     rowoff, col, val, X = graphs.build_config_torch(cfg_id, device, scale_down=scale_down)
     a, b = shards.shard_bounds(rowoff, costs.C_compute_ns + costs.C_load_ns, costs.C_store_ns,
                                world, rank)
+    bounds = [shards.shard_bounds(rowoff, costs.C_compute_ns + costs.C_load_ns,
+                                  costs.C_store_ns, world, r) for r in range(world)]
     e0, e1 = int(rowoff[a]), int(rowoff[b])
     ro = (rowoff[a:b + 1] - e0).contiguous()
     sub_col = col[e0:e1].contiguous()
     sub_val = val[e0:e1].contiguous()
     return dict(rowoff=ro, col=sub_col, val=sub_val, X=X, n=b - a, nnz=e1 - e0, row0=a,
+                bounds=bounds,
                 nnz_total=int(rowoff[-1]), n_total=rowoff.numel() - 1, K=X.shape[1],
                 distinct_cols=int(torch.unique(sub_col).numel()) if e1 > e0 else 0)
 
@@ -259,6 +267,8 @@ class _DevPtr:
 
 
 def run_step(ctx, wl, tasks, n_tasks, out, flags):
+    if wl.get("x_sharded"):
+        shards.gather_rows(wl["X"], wl["bounds"])
     ctx.spmm_mean_device(wl["n"], wl["nnz"], wl["sro"].data_ptr(), wl["scol"].data_ptr(),
                          wl["sval"].data_ptr(), wl["org"].data_ptr(), wl["X"].data_ptr(),
                          wl["X"].shape[0], wl["K"], tasks.data_ptr(), n_tasks, out.data_ptr(),
@@ -358,6 +368,14 @@ def run_ours(args):
     ctx.set_stream(torch.cuda.current_stream().cuda_stream)
     device_prepare(ctx, wl)
     K = wl["K"]
+    x_full = wl["X"]
+    if args.x_sharded and world > 1:
+        # X as a prior layer leaves it: this rank holds only its own rows; the
+        # rest is poisoned so that only the per-step all-gather can fill it.
+        a, b = wl["bounds"][rank]
+        xs = torch.full_like(x_full, float("nan"))
+        xs[a:b] = x_full[a:b]
+        wl.update(X=xs, x_sharded=True)
     out = torch.empty((max(wl["n"], 1), K), dtype=torch.float32, device=device)
 
     # S: the reference's --candidates procedure (main.cpp:534-577): three
@@ -408,6 +426,8 @@ def run_ours(args):
     barrier(world)
     clocks = sampler.stop() if sampler else None
     assert ctx.take_device_errors() == 0
+    if wl.get("x_sharded"):
+        assert torch.equal(wl["X"], x_full), "all-gathered X differs from the source"
     t_max = allreduce_max(t_local, world)
 
     flops_total = 2.0 * wl["nnz_total"] * K
@@ -460,6 +480,8 @@ def run_ours(args):
                        "rows": wl["n_total"], "nnz": wl["nnz_total"], "K": K, "S": S,
                        "n_tasks_rank0": n_tasks, "costs": os.path.relpath(COSTS_FILE, ROOT),
                        "parallelism": f"row shards x{world}" if world > 1 else "single GPU",
+                       "x": ("row-sharded; one NCCL all-gather per step, inside the timing"
+                             if wl.get("x_sharded") else "replicated"),
                        "l2": "inputs larger than L2 (CSR + X > 126 MB), no flush",
                        "hbm_gbs_rank0": round(achieved, 1),
                        "preprocess_ms_rank0": {"sort_by_degree": round(wl["sort_ms"], 3),

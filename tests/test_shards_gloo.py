@@ -79,3 +79,31 @@ def test_row_shards_reassemble_to_single_rank_result(tmp_path, oracle, world):
     from helpers import assert_mean_close
     assert gathered.shape == ref.shape
     assert_mean_close(gathered, ref, cond, what="sharded vs single")
+
+
+def _gather_worker(rank, world, port, out_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rowoff, col, val, X = _graph()
+        bounds = [shards.shard_bounds(rowoff, COSTS[0] + COSTS[1], COSTS[2], world, r)
+                  for r in range(world)]
+        # Each rank starts with only its own block (the rest poisoned).
+        x = torch.full(X.shape, float("nan"))
+        a, b = bounds[rank]
+        x[a:b] = torch.from_numpy(X[a:b])
+        shards.gather_rows(x, bounds)
+        np.save(out_path + f".{rank}.npy", x.numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gather_rows_rebuilds_the_sharded_input_on_every_rank(tmp_path, world):
+    out_path = str(tmp_path / "x")
+    mp.spawn(_gather_worker, args=(world, _free_port(), out_path), nprocs=world, join=True)
+    _, _, _, X = _graph()
+    for r in range(world):
+        got = np.load(out_path + f".{r}.npy")
+        assert np.array_equal(got, X), f"rank {r}"
