@@ -241,3 +241,35 @@ def test_spmm_bad_indices_raise_without_fault(ctx):
         ctx.spmmKernel(bad_origin, H, 16, 16, tasks)
     out, _ = ctx.spmmKernel(good, H, 16, 16, tasks)  # the context still works
     assert np.allclose(out[[3, 2, 0]], 1.0) and not out[1].any()
+
+
+@pytest.mark.parametrize("K", [7, 100, 512])
+def test_whole_rows_bit_exact(ctx, oracle, K):
+    """Widths whose kernels give every row to one lane group (K = 100 and 512:
+    one group per warp; K = 7: the scalar kernel) sum a whole row in nonzero
+    order with one FMA chain and divide once, exactly as the reference's
+    kernel (src/parallelMatrix.cpp:151-236): those rows are bit-identical to
+    the oracle's FP32 restatement.  Rows split across tasks differ only in the
+    order the fragments are added."""
+    rng = np.random.default_rng(100 + K)
+    n = 900
+    rowoff, col, val = random_csr(rng, n, 70, hubs=3, hub_factor=30)
+    H = rng.standard_normal((n, K)).astype(np.float32)
+    costs = [0.1, 0.6, 0.4, 0.9]
+    origin, srow, scol, sval, cap, tasks = _oracle_pipeline(oracle, rowoff, col, val, costs, 24)
+    order = cs.CSR_Order(srow, scol, sval, origin)
+    out, _ = ctx.spmmKernel(order, H, K, K, tasks)
+    o32 = oracle.spmm_mean(srow, scol, sval, origin, H, tasks)
+    deg = np.diff(srow)
+    whole = np.zeros(n, bool)
+    for rs, re_, fo, ln in np.asarray(tasks).reshape(-1, 4):
+        for r in range(rs, re_):
+            b = fo if r == rs else 0
+            e = ln if (r == re_ - 1 and ln > 0) else deg[r]
+            if b == 0 and e == deg[r]:
+                whole[r] = True
+    rows = origin[whole]
+    assert len(rows) > n // 2
+    assert np.array_equal(out[rows], o32[rows])
+    ref, cond = oracle.spmm_mean_f64(srow, scol, sval, origin, H)
+    assert_mean_close(out, ref, cond, what=f"K={K}")
