@@ -256,7 +256,8 @@ def test_whole_rows_bit_exact(ctx, oracle, K):
     rowoff, col, val = random_csr(rng, n, 70, hubs=3, hub_factor=30)
     H = rng.standard_normal((n, K)).astype(np.float32)
     costs = [0.1, 0.6, 0.4, 0.9]
-    origin, srow, scol, sval, cap, tasks = _oracle_pipeline(oracle, rowoff, col, val, costs, 24)
+    # S = 128: all rows but the three hubs are whole inside one task.
+    origin, srow, scol, sval, cap, tasks = _oracle_pipeline(oracle, rowoff, col, val, costs, 128)
     order = cs.CSR_Order(srow, scol, sval, origin)
     out, _ = ctx.spmmKernel(order, H, K, K, tasks)
     o32 = oracle.spmm_mean(srow, scol, sval, origin, H, tasks)
