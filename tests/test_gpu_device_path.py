@@ -85,21 +85,13 @@ def test_tasks_check_detects_gaps(ctx):
     assert ctx.tasks_check(4, 7, d_ro.data_ptr(), bad.data_ptr(), 1)["bad_tasks"] == 1
 
 
-def test_x_far_larger_than_l2(ctx):
-    """X of 2.3M x 256 floats (2.4 GB, far larger than L2; most gathers miss
-    L2), checked against a float64 reference computed on the device by torch."""
-    dev = torch.device("cuda:0")
-    g = torch.Generator(device=dev)
-    g.manual_seed(17)
-    n, h_rows, K = 20000, 2_300_000, 256
-    deg = torch.randint(0, 60, (n,), generator=g, device=dev)
-    deg[::997] = 700  # a few long rows (split into fragments)
+def _aggregate_vs_torch(ctx, n, h_rows, K, deg, col, val, X, S=64):
+    """Sort, partition and aggregate on the device through the C ABI; compare
+    with a float64 reference computed by torch on the device."""
+    dev = X.device
     rowoff = torch.zeros(n + 1, dtype=torch.int64, device=dev)
     rowoff[1:] = torch.cumsum(deg, 0)
     nnz = int(rowoff[-1])
-    col = torch.randint(0, h_rows, (nnz,), generator=g, device=dev, dtype=torch.int32)
-    val = torch.randn(nnz, generator=g, device=dev)
-    X = torch.randn((h_rows, K), generator=g, device=dev)
     ro32 = rowoff.to(torch.int32)
     org = torch.empty(n, dtype=torch.int32, device=dev)
     sro = torch.empty(n + 1, dtype=torch.int32, device=dev)
@@ -108,7 +100,7 @@ def test_x_far_larger_than_l2(ctx):
     ctx.sort_by_degree_device(n, nnz, ro32.data_ptr(), col.data_ptr(), val.data_ptr(),
                               org.data_ptr(), sro.data_ptr(), scol.data_ptr(), sval.data_ptr())
     costs = cs.SpmmCostParams(0.0055, 0.018, 0.011, 0.5)
-    t_ptr, n_tasks = ctx.partition_device(n, sro.data_ptr(), costs, cs.capacity_from_s(64, costs))
+    t_ptr, n_tasks = ctx.partition_device(n, sro.data_ptr(), costs, cs.capacity_from_s(S, costs))
     out = torch.full((n, K), float("nan"), device=dev)
     ctx.spmm_mean_device(n, nnz, sro.data_ptr(), scol.data_ptr(), sval.data_ptr(), org.data_ptr(),
                          X.data_ptr(), h_rows, K, t_ptr, n_tasks, out.data_ptr(), 0)
@@ -130,6 +122,47 @@ def test_x_far_larger_than_l2(ctx):
     bad = err > 1e-5 * scale
     bad &= ~((scale == 0) & (err == 0))
     assert int(bad.sum()) == 0, float((err / scale.clamp_min(1e-30)).max())
+
+
+def test_x_far_larger_than_l2(ctx):
+    """X of 2.3M x 256 floats (2.4 GB, far larger than L2; most gathers miss
+    L2), checked against a float64 reference computed on the device by torch."""
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(17)
+    n, h_rows, K = 20000, 2_300_000, 256
+    deg = torch.randint(0, 60, (n,), generator=g, device=dev)
+    deg[::997] = 700  # a few long rows (split into fragments)
+    nnz = int(deg.sum())
+    col = torch.randint(0, h_rows, (nnz,), generator=g, device=dev, dtype=torch.int32)
+    val = torch.randn(nnz, generator=g, device=dev)
+    X = torch.randn((h_rows, K), generator=g, device=dev)
+    _aggregate_vs_torch(ctx, n, h_rows, K, deg, col, val, X)
+
+
+@pytest.mark.parametrize("K", [256, 254])
+def test_x_beyond_2_pow_31_elements(ctx, K):
+    """X with more than 2^31 elements (8.6M x K floats, 8.8 GB), half of the
+    gathers aimed at its last 100K rows: element offsets past 2^31 must be
+    formed in 64 bits, in the float4 kernel (K = 256) and in the scalar one
+    (K = 254)."""
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(K)
+    n, h_rows = 5000, 8_600_000
+    assert h_rows * K > 2 ** 31
+    deg = torch.randint(0, 40, (n,), generator=g, device=dev)
+    deg[::499] = 400
+    nnz = int(deg.sum())
+    col = torch.randint(0, h_rows, (nnz,), generator=g, device=dev, dtype=torch.int32)
+    top = torch.randint(h_rows - 100_000, h_rows, (nnz,), generator=g, device=dev,
+                        dtype=torch.int32)
+    col = torch.where(torch.rand(nnz, generator=g, device=dev) < 0.5, top, col)
+    val = torch.randn(nnz, generator=g, device=dev)
+    X = torch.randn((h_rows, K), generator=g, device=dev)
+    _aggregate_vs_torch(ctx, n, h_rows, K, deg, col, val, X)
+    del X
+    torch.cuda.empty_cache()
 
 
 @pytest.mark.parametrize("K", [1, 7, 32, 300])
