@@ -34,6 +34,8 @@
 // task row outside [0, n_rows), non-monotone offsets or an origin outside
 // [0, n_rows) never fault: the entry is skipped and a CWLB_DEVERR_* bit is
 // raised in the context's device error word.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace cwlb {
@@ -91,6 +93,31 @@ __device__ __forceinline__ int row_fragment(const SpmmArgs& a, int r, const cwlb
         return 2;
     }
     f.orig = __ldg(a.origin + r);
+    if (f.orig < 0 || f.orig >= a.n_rows) {
+        raise_err(a.err, CWLB_DEVERR_ORIGIN_RANGE);
+        return 2;
+    }
+    f.base = b0;
+    f.deg = b1 - b0;
+    if (f.deg <= 0) return 1;
+    int32_t begin = (r == t.row_start) ? t.first_row_offset : 0;
+    int32_t end = f.deg;
+    if (r == t.row_end - 1 && t.last_row_nnz > 0) end = t.last_row_nnz;
+    begin = min(max(begin, 0), f.deg);
+    end = min(max(end, begin), f.deg);
+    f.begin = begin;
+    f.end = end;
+    return begin < end ? 0 : 2;
+}
+
+// row_fragment with the row's offsets and origin already at hand.
+__device__ __forceinline__ int row_fragment_at(const SpmmArgs& a, int r, const cwlb_task& t,
+                                               int32_t b0, int32_t b1, int32_t orig, RowFrag& f) {
+    if (b0 < 0 || b1 < b0 || b1 > a.nnz) {
+        raise_err(a.err, CWLB_DEVERR_OFFSETS);
+        return 2;
+    }
+    f.orig = orig;
     if (f.orig < 0 || f.orig >= a.n_rows) {
         raise_err(a.err, CWLB_DEVERR_ORIGIN_RANGE);
         return 2;
@@ -255,7 +282,10 @@ __device__ __forceinline__ void write_zero_row(const SpmmArgs& a, int32_t orig,
         if (ok[i]) __stcs(out4 + q[i], make_float4(0.f, 0.f, 0.f, 0.f));
 }
 
-template <int L, int V>
+// Rows of a task staged per warp in short-row mode (see launch_spmm_mean).
+constexpr int kStageRows = 128;
+
+template <int L, int V, bool kStage>
 __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
     constexpr int G = VecCfg<L, V>::G;
     const int lane = threadIdx.x & 31;
@@ -297,9 +327,37 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
         const int team_lanes = T * L;
         const unsigned tmask = team_lanes == 32 ? 0xffffffffu
                                                 : (((1u << team_lanes) - 1u) << (team * team_lanes));
+        // Short-row mode: the task's row offsets and origins are loaded with a
+        // few coalesced loads up front, so that no row waits on its own.
+        struct Staged {
+            int32_t ro[kWarpsPerCta][kStageRows + 1];
+            int32_t org[kWarpsPerCta][kStageRows];
+        };
+        __shared__ typename std::conditional<kStage, Staged, char>::type stage;
+        const int w = threadIdx.x >> 5;
+        bool staged = false;
+        if constexpr (kStage) {
+            staged = n_task_rows <= kStageRows;
+            if (staged) {
+                for (int i = lane; i <= n_task_rows; i += 32)
+                    stage.ro[w][i] = __ldg(a.rowoff + tk.row_start + i);
+                for (int i = lane; i < n_task_rows; i += 32)
+                    stage.org[w][i] = __ldg(a.origin + tk.row_start + i);
+                __syncwarp();
+            }
+        }
         for (int r = tk.row_start + team; r < tk.row_end; r += teams) {
             RowFrag f;
-            const int st = row_fragment(a, r, tk, f);
+            int st;
+            if constexpr (kStage) {
+                const int i = r - tk.row_start;
+                st = staged ? row_fragment_at(a, r, tk, stage.ro[w][i], stage.ro[w][i + 1],
+                                              stage.org[w][i], f)
+                            : row_fragment(a, r, tk, f);
+            } else {
+                (void)w;
+                st = row_fragment(a, r, tk, f);
+            }
             if (st == 1) {
                 if (a.write_empty && gt == 0) write_zero_row<V>(a, f.orig, q, ok);
                 continue;
@@ -468,21 +526,25 @@ __global__ void __launch_bounds__(kThreads) zero_split_rows_kernel(SpmmArgs a) {
 }
 
 template <int L, int V>
-void launch_vec(const SpmmArgs& a, cudaStream_t s) {
+void launch_vec(const SpmmArgs& a, bool stage, cudaStream_t s) {
     const int64_t K4 = a.K >> 2;
     const int64_t tiles = ceil_div(K4, L * V);
     dim3 grid(static_cast<unsigned>(ceil_div(a.n_tasks, kWarpsPerCta)),
               static_cast<unsigned>(tiles));
-    spmm_vec_kernel<L, V><<<grid, kThreads, 0, s>>>(a);
+    if (stage) {
+        spmm_vec_kernel<L, V, true><<<grid, kThreads, 0, s>>>(a);
+    } else {
+        spmm_vec_kernel<L, V, false><<<grid, kThreads, 0, s>>>(a);
+    }
 }
 
 template <int L>
-void launch_vec_v(int V, const SpmmArgs& a, cudaStream_t s) {
+void launch_vec_v(int V, const SpmmArgs& a, bool stage, cudaStream_t s) {
     switch (V) {
-        case 1: launch_vec<L, 1>(a, s); break;
-        case 2: launch_vec<L, 2>(a, s); break;
-        case 3: launch_vec<L, 3>(a, s); break;
-        default: launch_vec<L, 4>(a, s); break;
+        case 1: launch_vec<L, 1>(a, stage, s); break;
+        case 2: launch_vec<L, 2>(a, stage, s); break;
+        case 3: launch_vec<L, 3>(a, stage, s); break;
+        default: launch_vec<L, 4>(a, stage, s); break;
     }
 }
 
@@ -558,13 +620,19 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
     if (aligned) {
         int L = 32, V = 1;
         pick_vec_shape(K >> 2, L, V);
+        // Short-row mode when tasks hold many rows on average (>= 16, e.g.
+        // configuration 4's degree-4 rows, ~54 rows per task): each row's
+        // offsets would otherwise be a dependent load on its critical path.
+        // It costs 8 KB of shared memory per CTA, taken from L1, so
+        // hub-heavy graphs with few rows per task keep the plain kernel.
+        const bool stage = static_cast<int64_t>(n_rows) >= 16 * n_tasks;
         switch (L) {
-            case 1: launch_vec_v<1>(V, a, s); break;
-            case 2: launch_vec_v<2>(V, a, s); break;
-            case 4: launch_vec_v<4>(V, a, s); break;
-            case 8: launch_vec_v<8>(V, a, s); break;
-            case 16: launch_vec_v<16>(V, a, s); break;
-            default: launch_vec_v<32>(V, a, s); break;
+            case 1: launch_vec_v<1>(V, a, stage, s); break;
+            case 2: launch_vec_v<2>(V, a, stage, s); break;
+            case 4: launch_vec_v<4>(V, a, stage, s); break;
+            case 8: launch_vec_v<8>(V, a, stage, s); break;
+            case 16: launch_vec_v<16>(V, a, stage, s); break;
+            default: launch_vec_v<32>(V, a, stage, s); break;
         }
         CWLB_LAUNCH_CHECK("spmm_vec_kernel");
     } else {

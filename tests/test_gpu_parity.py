@@ -274,3 +274,38 @@ def test_whole_rows_bit_exact(ctx, oracle, K):
     assert np.array_equal(out[rows], o32[rows])
     ref, cond = oracle.spmm_mean_f64(srow, scol, sval, origin, H)
     assert_mean_close(out, ref, cond, what=f"K={K}")
+
+
+@pytest.mark.parametrize("K", [4, 32, 64, 128, 512])
+def test_short_row_mode_vs_oracle(ctx, oracle, K):
+    """Many short rows per task (~117 here, >= 16 on average) select the
+    kernel's short-row mode (a task's row offsets and origins loaded up front,
+    tasks of more than 128 rows falling back per row).  Whole rows of tasks
+    with at least 32 rows go to one lane group each: bit-identical to the
+    oracle's FP32 restatement; the rest within the tolerance."""
+    rng = np.random.default_rng(7 + K)
+    n = 6000
+    rowoff, col, val = random_csr(rng, n, 4, hubs=2, hub_factor=300)
+    H = rng.standard_normal((n, K)).astype(np.float32)
+    costs = [0.1, 0.6, 0.4, 0.9]
+    origin, srow, scol, sval, cap, tasks = _oracle_pipeline(oracle, rowoff, col, val, costs, 300)
+    tk = np.asarray(tasks).reshape(-1, 4)
+    assert n >= 16 * len(tk)                      # short-row mode
+    assert (tk[:, 1] - tk[:, 0] > 128).any()      # and some tasks beyond the staging size
+    order = cs.CSR_Order(srow, scol, sval, origin)
+    out, _ = ctx.spmmKernel(order, H, K, K, tasks)
+    ref, cond = oracle.spmm_mean_f64(srow, scol, sval, origin, H)
+    assert_mean_close(out, ref, cond, what=f"K={K}")
+    o32 = oracle.spmm_mean(srow, scol, sval, origin, H, tasks)
+    deg = np.diff(srow)
+    exact = []
+    for rs, re_, fo, ln in tk:
+        if re_ - rs < 32:
+            continue
+        for r in range(rs, re_):
+            b = fo if r == rs else 0
+            e = ln if (r == re_ - 1 and ln > 0) else deg[r]
+            if b == 0 and e == deg[r]:
+                exact.append(origin[r])
+    assert len(exact) > n // 2
+    assert np.array_equal(out[exact], o32[exact])
