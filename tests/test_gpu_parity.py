@@ -309,3 +309,27 @@ def test_short_row_mode_vs_oracle(ctx, oracle, K):
                 exact.append(origin[r])
     assert len(exact) > n // 2
     assert np.array_equal(out[exact], o32[exact])
+
+
+def test_empty_graphs(ctx, oracle):
+    """No rows, and rows without nonzeros, through sort, partition and
+    aggregation: the same (empty or all-zero) results as the oracle."""
+    costs = cs.SpmmCostParams(0.1, 0.6, 0.4, 0.9)
+    # No rows at all.
+    empty = cs.CSR(np.zeros(1, np.int32), np.zeros(0, np.int32), np.zeros(0, np.float32))
+    order = ctx.sortCSRByDegree(empty)
+    assert len(order.Origin_local) == 0
+    tasks = ctx.costWeightedTaskPartitioning(order, costs, cs.capacity_from_s(8, costs))
+    assert len(tasks) == 0
+    # Rows without nonzeros.
+    ro = np.zeros(37, np.int32)
+    csr = cs.CSR(ro, np.zeros(0, np.int32), np.zeros(0, np.float32))
+    order = ctx.sortCSRByDegree(csr)
+    o = oracle.sort_by_degree(ro, np.zeros(0, np.int32), np.zeros(0, np.float32))
+    assert np.array_equal(order.Origin_local, o[0]) and np.array_equal(order.RowOffset, o[1])
+    cap = cs.capacity_from_s(8, costs)
+    tasks = ctx.costWeightedTaskPartitioning(order, costs, cap)
+    want = oracle.partition(o[1], [0.1, 0.6, 0.4, 0.9], cap)
+    assert np.array_equal(tasks, want)
+    out, _ = ctx.spmmKernel(order, np.ones((36, 8), np.float32), 8, 8, tasks)
+    assert out.shape == (36, 8) and not out.any()
