@@ -3,6 +3,7 @@
 // function converts internal failures into a cwlb_status and a thread-local
 // message; no C++ exception crosses the boundary.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <filesystem>
@@ -10,6 +11,8 @@
 #include <iomanip>
 #include <limits>
 #include <string>
+#include <thread>
+#include <vector>
 
 #include "common.cuh"
 
@@ -69,6 +72,65 @@ void raise_device_errors(uint32_t flags) {
     cwlb::fail(CWLB_ERR_INVALID_ARGUMENT, m);
 }
 
+// True when every value is exactly 1.0f (the reference's text loader gives
+// every stored entry the value 1, src/data.cpp).  Scans with up to 16 host
+// threads and stops at the first other value.
+bool all_ones(const float* v, size_t n) {
+    if (n == 0) return true;
+    constexpr uint32_t kOne = 0x3f800000u;
+    const size_t per_thread_min = size_t(1) << 20;
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const unsigned T = static_cast<unsigned>(
+        std::min<size_t>(std::min(16u, hw), (n + per_thread_min - 1) / per_thread_min));
+    std::atomic<bool> other{false};
+    auto scan = [&](size_t b, size_t e) {
+        constexpr size_t kBlock = size_t(1) << 16;
+        for (size_t i = b; i < e; i += kBlock) {
+            if (other.load(std::memory_order_relaxed)) return;
+            const size_t end = std::min(e, i + kBlock);
+            uint32_t acc = 0;
+            for (size_t j = i; j < end; ++j) {
+                uint32_t w;
+                std::memcpy(&w, v + j, sizeof(w));
+                acc |= w ^ kOne;
+            }
+            if (acc) {
+                other.store(true, std::memory_order_relaxed);
+                return;
+            }
+        }
+    };
+    if (T <= 1) {
+        scan(0, n);
+    } else {
+        std::vector<std::thread> pool;
+        const size_t chunk = (n + T - 1) / T;
+        for (unsigned t = 1; t < T; ++t) {
+            const size_t b = std::min(n, t * chunk);
+            pool.emplace_back(scan, b, std::min(n, b + chunk));
+        }
+        scan(0, std::min(n, chunk));
+        for (auto& th : pool) th.join();
+    }
+    return !other.load();
+}
+
+// Device copy of the values: unit values are not copied (a device array of
+// ones, kept by the context, stands in for them: the kernels' arithmetic and
+// results are the same), others are staged as usual.  The check runs on the
+// host while the copies issued before it are in flight.
+const float* stage_values(cwlb_ctx* ctx, const float* value, size_t nnz) {
+    if (nnz && all_ones(value, nnz)) {
+        if (ctx->ones_count < nnz) {
+            float* d = ctx->ones.as<float>(nnz);
+            cwlb::launch_fill_ones(ctx, d, nnz);
+            ctx->ones_count = nnz;
+        }
+        return static_cast<const float*>(ctx->ones.ptr);
+    }
+    return stage_h2d(ctx, ctx->in_val, value, nnz);
+}
+
 // Shared body of cwlb_spmm_kernel / cwlb_spmm_kernel_large_k.
 void spmm_host(cwlb_ctx* ctx, bool large_k, int32_t n_rows, int32_t nnz,
                const int32_t* row_offset, const int32_t* col_ind, const float* value,
@@ -117,10 +179,10 @@ void spmm_host(cwlb_ctx* ctx, bool large_k, int32_t n_rows, int32_t nnz,
 
     const int32_t* d_ro = stage_h2d(ctx, ctx->in_rowoff, row_offset, static_cast<size_t>(n_rows) + 1);
     const int32_t* d_col = stage_h2d(ctx, ctx->in_col, col_ind, static_cast<size_t>(nnz));
-    const float* d_val = stage_h2d(ctx, ctx->in_val, value, static_cast<size_t>(nnz));
     const int32_t* d_org = stage_h2d(ctx, ctx->in_origin, origin, static_cast<size_t>(n_rows));
     const float* d_H = stage_h2d(ctx, ctx->in_H, H, static_cast<size_t>(h_rows) * K);
     const cwlb_task* d_tasks = stage_h2d(ctx, ctx->in_tasks, tasks, static_cast<size_t>(n_tasks));
+    const float* d_val = stage_values(ctx, value, static_cast<size_t>(nnz));
     float* d_out = ctx->out_buf.as<float>(out_count);
 
     CWLB_CUDA(cudaEventRecord(ctx->ev_start, ctx->stream));
@@ -194,7 +256,7 @@ int cwlb_ctx_destroy(cwlb_ctx* ctx) {
         for (cwlb::DeviceBuffer* b : {&ctx->in_rowoff, &ctx->in_col, &ctx->in_val, &ctx->in_origin,
                                       &ctx->in_H, &ctx->in_tasks, &ctx->out_buf, &ctx->sort_scratch,
                                       &ctx->part_scratch, &ctx->part_desc, &ctx->part_tasks,
-                                      &ctx->check_scratch})
+                                      &ctx->check_scratch, &ctx->ones})
             b->release();
         if (ctx->d_error_flags) cudaFree(ctx->d_error_flags);
         if (ctx->ev_start) cudaEventDestroy(ctx->ev_start);

@@ -70,6 +70,9 @@ struct cwlb_ctx {
     // device) and for the sort / partition pipelines.
     cwlb::DeviceBuffer in_rowoff, in_col, in_val, in_origin, in_H, in_tasks, out_buf;
     cwlb::DeviceBuffer sort_scratch, part_scratch, part_desc, part_tasks, check_scratch;
+    // 1.0f values for host-buffer calls whose values are all one (not copied).
+    cwlb::DeviceBuffer ones;
+    size_t ones_count = 0;
 };
 
 namespace cwlb {
@@ -79,6 +82,8 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
                       const int32_t* col, const float* val, const int32_t* origin,
                       const float* H, int64_t h_rows, int64_t K, const cwlb_task* tasks,
                       int64_t n_tasks, float* out, uint32_t flags);
+// Writes `count` floats of 1.0f (spmm.cu).
+void launch_fill_ones(cwlb_ctx* ctx, float* dst, size_t count);
 // Float64 reference of the aggregation over an unsorted CSR (spmm.cu).
 void launch_spmm_mean_reference(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                                 const int32_t* col, const float* val, const float* H,

@@ -34,6 +34,7 @@
 // task row outside [0, n_rows), non-monotone offsets or an origin outside
 // [0, n_rows) never fault: the entry is skipped and a CWLB_DEVERR_* bit is
 // raised in the context's device error word.
+#include <algorithm>
 #include <type_traits>
 
 #include "common.cuh"
@@ -703,6 +704,24 @@ spmm_mean_reference_kernel(const int32_t* __restrict__ rowoff, const int32_t* __
 }
 
 }  // namespace
+
+namespace {
+__global__ void fill_ones_kernel(float* __restrict__ dst, size_t count) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+         i += stride)
+        dst[i] = 1.0f;
+}
+}  // namespace
+
+void launch_fill_ones(cwlb_ctx* ctx, float* dst, size_t count) {
+    if (count == 0) return;
+    const unsigned blocks = static_cast<unsigned>(
+        std::min<int64_t>(ceil_div(static_cast<int64_t>(count), kThreads),
+                          static_cast<int64_t>(ctx->props.multiProcessorCount) * 8));
+    fill_ones_kernel<<<blocks, kThreads, 0, ctx->stream>>>(dst, count);
+    CWLB_LAUNCH_CHECK("fill_ones_kernel");
+}
 
 void launch_spmm_mean_reference(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                                 const int32_t* col, const float* val, const float* H,

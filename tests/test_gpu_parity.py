@@ -333,3 +333,35 @@ def test_empty_graphs(ctx, oracle):
     assert np.array_equal(tasks, want)
     out, _ = ctx.spmmKernel(order, np.ones((36, 8), np.float32), 8, 8, tasks)
     assert out.shape == (36, 8) and not out.any()
+
+
+def test_unit_values_are_not_copied_but_give_the_same_result(ctx, oracle):
+    """Host-buffer calls whose values are all 1.0 (what the reference's loader
+    produces) do not copy the values: a device array of ones stands in.  The
+    result is the same as the oracle's; a single other value anywhere (start,
+    thread-chunk boundaries, end of a multi-million array) is detected."""
+    # A small unit-valued call first; the large ones below grow the array of ones.
+    small = cs.CSR_Order(np.array([0, 2, 3], np.int32), np.array([0, 1, 1], np.int32),
+                         np.ones(3, np.float32), np.array([1, 0], np.int32))
+    out, _ = ctx.spmmKernel(small, np.arange(8, dtype=np.float32).reshape(2, 4), 4, 4,
+                            np.array([[0, 2, 0, 0]], np.int32))
+    assert np.array_equal(out, np.array([[4, 5, 6, 7], [2, 3, 4, 5]], np.float32))
+    rng = np.random.default_rng(77)
+    n, K = 40000, 32
+    rowoff, col, _ = random_csr(rng, n, 150, hubs=2, hub_factor=20)
+    nnz = len(col)
+    assert nnz > 2_000_000
+    H = rng.standard_normal((n, K)).astype(np.float32)
+    costs = [0.1, 0.6, 0.4, 0.9]
+    ones = np.ones(nnz, np.float32)
+    origin, srow, scol, sval, cap, tasks = _oracle_pipeline(oracle, rowoff, col, ones, costs, 128)
+    for pos in [None, 0, nnz // 3, nnz // 2, (2 * nnz) // 3, nnz - 1]:
+        v = sval.copy()
+        if pos is not None:
+            v[pos] = 2.0
+        order = cs.CSR_Order(srow, scol, v, origin)
+        out, _ = ctx.spmmKernel(order, H, K, K, tasks)
+        ref, cond = oracle.spmm_mean_f64(srow, scol, v, origin, H)
+        assert_mean_close(out, ref, cond, what=f"pos={pos}")
+        o32 = oracle.spmm_mean(srow, scol, v, origin, H, tasks)
+        assert np.abs(out - o32).max() <= 1e-4
