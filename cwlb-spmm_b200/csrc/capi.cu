@@ -115,20 +115,131 @@ bool all_ones(const float* v, size_t n) {
     return !other.load();
 }
 
-// Device copy of the values: unit values are not copied (a device array of
-// ones, kept by the context, stands in for them: the kernels' arithmetic and
-// results are the same), others are staged as usual.  The check runs on the
-// host while the copies issued before it are in flight.
-const float* stage_values(cwlb_ctx* ctx, const float* value, size_t nnz) {
-    if (nnz && all_ones(value, nnz)) {
-        if (ctx->ones_count < nnz) {
-            float* d = ctx->ones.as<float>(nnz);
-            cwlb::launch_fill_ones(ctx, d, nnz);
-            ctx->ones_count = nnz;
-        }
-        return static_cast<const float*>(ctx->ones.ptr);
+// Chunked copy plan for a host-buffer call: chunk c holds tasks
+// [task_cut[c], task_cut[c+1]) and needs nonzeros [0, nnz_cut[c+1]).  Possible
+// when every task's rows are in range and the tasks are in order of their
+// last nonzero (as the partitioner emits them); small calls are not split.
+bool plan_pipeline(const int32_t* row_offset, int32_t n_rows, int32_t nnz, const cwlb_task* tasks,
+                   int64_t n_tasks, int64_t (&task_cut)[cwlb_ctx::kPipeChunks + 1],
+                   int64_t (&nnz_cut)[cwlb_ctx::kPipeChunks + 1]) {
+    constexpr int C = cwlb_ctx::kPipeChunks;
+    if (nnz < (1 << 22) || n_tasks < 8 * C) return false;
+    std::vector<int64_t> last(static_cast<size_t>(n_tasks));
+    int64_t prev = 0;
+    for (int64_t t = 0; t < n_tasks; ++t) {
+        const cwlb_task& k = tasks[t];
+        if (k.row_start < 0 || k.row_end > n_rows || k.row_start >= k.row_end) return false;
+        const int64_t b = row_offset[k.row_end - 1], e = row_offset[k.row_end];
+        if (b < 0 || e < b || e > nnz) return false;
+        const int64_t end = k.last_row_nnz > 0 ? std::min<int64_t>(e, b + k.last_row_nnz) : e;
+        if (end < prev) return false;
+        last[static_cast<size_t>(t)] = prev = end;
     }
-    return stage_h2d(ctx, ctx->in_val, value, nnz);
+    task_cut[0] = 0;
+    nnz_cut[0] = 0;
+    for (int c = 1; c < C; ++c) {
+        const int64_t target = static_cast<int64_t>(nnz) * c / C;
+        int64_t t = std::upper_bound(last.begin(), last.end(), target) - last.begin();
+        t = std::max(t, task_cut[c - 1]);
+        task_cut[c] = t;
+        nnz_cut[c] = t > 0 ? last[static_cast<size_t>(t - 1)] : 0;
+    }
+    task_cut[C] = n_tasks;
+    nnz_cut[C] = nnz;
+    return true;
+}
+
+template <typename T>
+void copy_h2d(T* dst, const T* src, int64_t count, cudaStream_t s) {
+    if (count > 0) {
+        CWLB_CUDA(cudaMemcpyAsync(dst, src, sizeof(T) * static_cast<size_t>(count),
+                                  cudaMemcpyHostToDevice, s));
+    }
+}
+
+// Host-buffer aggregation.  All copies go on the context's copy stream: the
+// row offsets, origins, tasks and X first, then the column ids in chunks (see
+// plan_pipeline; one chunk when the tasks cannot be chunked), then the values
+// unless they are all one (checked on the host while the copies run).  The
+// compute stream aggregates chunk c's tasks as soon as chunk c has arrived,
+// while later chunks are still being copied.  `time_us` is the sum of the
+// aggregation kernels' times.
+void spmm_host_staged(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* row_offset,
+                      const int32_t* col_ind, const float* value, const int32_t* origin,
+                      const float* H, int64_t h_rows, int64_t K, const cwlb_task* tasks,
+                      int64_t n_tasks, float* out, double* time_us) {
+    constexpr int C = cwlb_ctx::kPipeChunks;
+    cudaStream_t cs = ctx->copy_stream, ks = ctx->stream;
+    const size_t out_count = static_cast<size_t>(n_rows) * static_cast<size_t>(K);
+    int32_t* d_ro = ctx->in_rowoff.as<int32_t>(static_cast<size_t>(n_rows) + 1);
+    int32_t* d_col = ctx->in_col.as<int32_t>(static_cast<size_t>(nnz));
+    int32_t* d_org = ctx->in_origin.as<int32_t>(static_cast<size_t>(n_rows));
+    float* d_H = ctx->in_H.as<float>(static_cast<size_t>(h_rows) * static_cast<size_t>(K));
+    cwlb_task* d_tasks = ctx->in_tasks.as<cwlb_task>(static_cast<size_t>(n_tasks));
+    float* d_out = ctx->out_buf.as<float>(out_count);
+    bool launched[C] = {};
+    int n_chunks = 1;
+    try {
+        // Copies start after whatever the compute stream has queued.
+        CWLB_CUDA(cudaEventRecord(ctx->ev_start, ks));
+        CWLB_CUDA(cudaStreamWaitEvent(cs, ctx->ev_start, 0));
+        copy_h2d(d_ro, row_offset, static_cast<int64_t>(n_rows) + 1, cs);
+        copy_h2d(d_org, origin, n_rows, cs);
+        copy_h2d(d_tasks, tasks, n_tasks, cs);
+        copy_h2d(d_H, H, h_rows * K, cs);
+        int64_t task_cut[C + 1] = {0, n_tasks}, nnz_cut[C + 1] = {0, nnz};
+        if (plan_pipeline(row_offset, n_rows, nnz, tasks, n_tasks, task_cut, nnz_cut)) n_chunks = C;
+        for (int c = 0; c < n_chunks; ++c) {
+            copy_h2d(d_col + nnz_cut[c], col_ind + nnz_cut[c], nnz_cut[c + 1] - nnz_cut[c], cs);
+            CWLB_CUDA(cudaEventRecord(ctx->pipe_ready[c], cs));
+        }
+        const float* d_val = nullptr;
+        if (all_ones(value, static_cast<size_t>(nnz))) {
+            if (ctx->ones_count < static_cast<size_t>(nnz)) {
+                float* d = ctx->ones.as<float>(static_cast<size_t>(nnz));
+                cwlb::launch_fill_ones(ctx, d, static_cast<size_t>(nnz));
+                ctx->ones_count = static_cast<size_t>(nnz);
+            }
+            d_val = static_cast<const float*>(ctx->ones.ptr);
+        } else {
+            float* dv = ctx->in_val.as<float>(static_cast<size_t>(nnz));
+            for (int c = 0; c < n_chunks; ++c) {
+                copy_h2d(dv + nnz_cut[c], value + nnz_cut[c], nnz_cut[c + 1] - nnz_cut[c], cs);
+                CWLB_CUDA(cudaEventRecord(ctx->pipe_ready[c], cs));  // now after the values
+            }
+            d_val = dv;
+        }
+        if (out_count) CWLB_CUDA(cudaMemsetAsync(d_out, 0, sizeof(float) * out_count, ks));
+        for (int c = 0; c < n_chunks; ++c) {
+            const int64_t t0 = task_cut[c], nt = task_cut[c + 1] - task_cut[c];
+            if (nt <= 0) continue;
+            CWLB_CUDA(cudaStreamWaitEvent(ks, ctx->pipe_ready[c], 0));
+            CWLB_CUDA(cudaEventRecord(ctx->pipe_t0[c], ks));
+            cwlb::launch_spmm_mean(ctx, n_rows, nnz, d_ro, d_col, d_val, d_org, d_H, h_rows, K,
+                                   d_tasks + t0, nt, d_out, cwlb::kFlagOutCleared);
+            CWLB_CUDA(cudaEventRecord(ctx->pipe_t1[c], ks));
+            launched[c] = true;
+        }
+        if (out_count) {
+            CWLB_CUDA(cudaMemcpyAsync(out, d_out, sizeof(float) * out_count,
+                                      cudaMemcpyDeviceToHost, ks));
+        }
+    } catch (...) {
+        // No copy may still read the caller's arrays once the call returns.
+        cudaStreamSynchronize(cs);
+        cudaStreamSynchronize(ks);
+        throw;
+    }
+    CWLB_CUDA(cudaStreamSynchronize(cs));
+    raise_device_errors(take_device_errors(ctx));
+    double us = 0.0;
+    for (int c = 0; c < n_chunks; ++c) {
+        if (!launched[c]) continue;
+        float ms = 0.0f;
+        CWLB_CUDA(cudaEventElapsedTime(&ms, ctx->pipe_t0[c], ctx->pipe_t1[c]));
+        us += static_cast<double>(ms) * 1e3;
+    }
+    *time_us = us;
 }
 
 // Shared body of cwlb_spmm_kernel / cwlb_spmm_kernel_large_k.
@@ -177,26 +288,8 @@ void spmm_host(cwlb_ctx* ctx, bool large_k, int32_t n_rows, int32_t nnz,
                 (h_rows * K == 0 || H),
             CWLB_ERR_INVALID_ARGUMENT, "null input pointer");
 
-    const int32_t* d_ro = stage_h2d(ctx, ctx->in_rowoff, row_offset, static_cast<size_t>(n_rows) + 1);
-    const int32_t* d_col = stage_h2d(ctx, ctx->in_col, col_ind, static_cast<size_t>(nnz));
-    const int32_t* d_org = stage_h2d(ctx, ctx->in_origin, origin, static_cast<size_t>(n_rows));
-    const float* d_H = stage_h2d(ctx, ctx->in_H, H, static_cast<size_t>(h_rows) * K);
-    const cwlb_task* d_tasks = stage_h2d(ctx, ctx->in_tasks, tasks, static_cast<size_t>(n_tasks));
-    const float* d_val = stage_values(ctx, value, static_cast<size_t>(nnz));
-    float* d_out = ctx->out_buf.as<float>(out_count);
-
-    CWLB_CUDA(cudaEventRecord(ctx->ev_start, ctx->stream));
-    cwlb::launch_spmm_mean(ctx, n_rows, nnz, d_ro, d_col, d_val, d_org, d_H, h_rows, K, d_tasks,
-                           n_tasks, d_out, 0u);
-    CWLB_CUDA(cudaEventRecord(ctx->ev_stop, ctx->stream));
-    if (out_count) {
-        CWLB_CUDA(cudaMemcpyAsync(out, d_out, sizeof(float) * out_count, cudaMemcpyDeviceToHost,
-                                  ctx->stream));
-    }
-    raise_device_errors(take_device_errors(ctx));
-    float ms = 0.0f;
-    CWLB_CUDA(cudaEventElapsedTime(&ms, ctx->ev_start, ctx->ev_stop));
-    *time_us = static_cast<double>(ms) * 1e3;
+    spmm_host_staged(ctx, n_rows, nnz, row_offset, col_ind, value, origin, H, h_rows, K, tasks,
+                     n_tasks, out, time_us);
 }
 
 cwlb_costs zero_costs() {
@@ -238,6 +331,12 @@ int cwlb_ctx_create(int device, cwlb_ctx** out) {
             ctx->own_stream = true;
             CWLB_CUDA(cudaEventCreate(&ctx->ev_start));
             CWLB_CUDA(cudaEventCreate(&ctx->ev_stop));
+            CWLB_CUDA(cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking));
+            for (int c = 0; c < cwlb_ctx::kPipeChunks; ++c) {
+                CWLB_CUDA(cudaEventCreateWithFlags(&ctx->pipe_ready[c], cudaEventDisableTiming));
+                CWLB_CUDA(cudaEventCreate(&ctx->pipe_t0[c]));
+                CWLB_CUDA(cudaEventCreate(&ctx->pipe_t1[c]));
+            }
             CWLB_CUDA(cudaMalloc(&ctx->d_error_flags, sizeof(uint32_t)));
             CWLB_CUDA(cudaMemset(ctx->d_error_flags, 0, sizeof(uint32_t)));
         } catch (...) {
@@ -259,8 +358,15 @@ int cwlb_ctx_destroy(cwlb_ctx* ctx) {
                                       &ctx->check_scratch, &ctx->ones})
             b->release();
         if (ctx->d_error_flags) cudaFree(ctx->d_error_flags);
+        if (ctx->copy_stream) cudaStreamSynchronize(ctx->copy_stream);
         if (ctx->ev_start) cudaEventDestroy(ctx->ev_start);
         if (ctx->ev_stop) cudaEventDestroy(ctx->ev_stop);
+        for (int c = 0; c < cwlb_ctx::kPipeChunks; ++c) {
+            if (ctx->pipe_ready[c]) cudaEventDestroy(ctx->pipe_ready[c]);
+            if (ctx->pipe_t0[c]) cudaEventDestroy(ctx->pipe_t0[c]);
+            if (ctx->pipe_t1[c]) cudaEventDestroy(ctx->pipe_t1[c]);
+        }
+        if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
         if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
         delete ctx;
     });

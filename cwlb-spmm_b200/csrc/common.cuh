@@ -65,6 +65,12 @@ struct cwlb_ctx {
     bool own_stream = false;
     cudaDeviceProp props{};
     cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
+    // Host-buffer calls copy their inputs on copy_stream in chunks and start
+    // aggregating each chunk's tasks on `stream` as soon as it has arrived.
+    static constexpr int kPipeChunks = 8;
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t pipe_ready[kPipeChunks] = {};
+    cudaEvent_t pipe_t0[kPipeChunks] = {}, pipe_t1[kPipeChunks] = {};
     uint32_t* d_error_flags = nullptr;  // CWLB_DEVERR_* bits raised by kernels
     // Scratch for the host-buffer entry points (inputs/outputs staged on the
     // device) and for the sort / partition pipelines.
@@ -76,6 +82,9 @@ struct cwlb_ctx {
 };
 
 namespace cwlb {
+
+// launch_spmm_mean flag (internal): the caller has already zeroed `out`.
+constexpr uint32_t kFlagOutCleared = 1u << 31;
 
 // Launchers implemented in the .cu files (all asynchronous on ctx->stream).
 void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,

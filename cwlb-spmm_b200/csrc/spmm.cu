@@ -588,7 +588,7 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
     if (K <= 0 || n_rows <= 0) return;
     cudaStream_t s = ctx->stream;
     const bool covered = (flags & CWLB_ROWS_COVERED) != 0;
-    if (!covered) {
+    if (!covered && !(flags & kFlagOutCleared)) {
         CWLB_CUDA(cudaMemsetAsync(out, 0, sizeof(float) * static_cast<size_t>(n_rows) * K, s));
     }
     if (n_tasks <= 0) return;
