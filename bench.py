@@ -195,6 +195,18 @@ def allreduce_max(x, world):
     return float(t.item())
 
 
+def allgather_values(x, world):
+    """Every rank's value of x, in rank order (collective; all ranks call it)."""
+    if world == 1:
+        return [x]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(v.item()) for v in out]
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -429,6 +441,7 @@ def run_ours(args):
     if wl.get("x_sharded"):
         assert torch.equal(wl["X"], x_full), "all-gathered X differs from the source"
     t_max = allreduce_max(t_local, world)
+    per_rank_ms = [round(v / args.steps * 1e3, 4) for v in allgather_values(t_local, world)]
 
     flops_total = 2.0 * wl["nnz_total"] * K
     value = flops_total / (t_max / args.steps) / 1e9
@@ -484,6 +497,7 @@ def run_ours(args):
                        "rows": wl["n_total"], "nnz": wl["nnz_total"], "K": K, "S": S,
                        "n_tasks_rank0": n_tasks, "costs": os.path.relpath(COSTS_FILE, ROOT),
                        "parallelism": f"row shards x{world}" if world > 1 else "single GPU",
+                       "ms_per_step_by_rank": per_rank_ms,
                        "x": ("row-sharded; one NCCL all-gather per step, inside the timing"
                              if wl.get("x_sharded") else "replicated"),
                        "l2": "inputs larger than L2 (CSR + X > 126 MB), no flush",
