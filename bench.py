@@ -510,7 +510,12 @@ def run_ours(args):
                          "traffic": measured_traffic(f"config {args.config}: {cfg['name']}")
                          if args.scale_down == 1 and world == 1 else None,
                          "algorithmic_bytes_per_launch": bytes_local,
-                         "launch_us": round(per_launch * 1e6, 2)},
+                         "launch_us": round(per_launch * 1e6, 2),
+                         # Secondary ceilings: X rows gathered (4 nnz K bytes,
+                         # mostly served by L2) and FP32 FMAs (nnz K).
+                         "gather_bytes_per_launch": 4 * wl["nnz"] * K,
+                         "gather_tb_s": round(4 * wl["nnz"] * K / per_launch / 1e12, 2),
+                         "fma_per_launch": wl["nnz"] * K},
             "e2e": e2e,
             "gpu_launches": (2 if flags else 1) * args.steps,
             "clocks": clocks,
