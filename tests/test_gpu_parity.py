@@ -367,14 +367,14 @@ def test_unit_values_are_not_copied_but_give_the_same_result(ctx, oracle):
         assert np.abs(out - o32).max() <= 1e-4
 
 
-@pytest.mark.parametrize("unit", [True, False])
-def test_chunked_host_call_matches_single_shot(ctx, oracle, unit):
+@pytest.mark.parametrize("unit,K", [(True, 16), (False, 16), (True, 1100)])
+def test_chunked_host_call_matches_single_shot(ctx, oracle, unit, K):
     """Host-buffer calls of 4M+ nonzeros with tasks in partition order copy
     their nonzeros in chunks and aggregate each chunk as soon as it arrives.
     The same tasks in reverse order cannot be chunked (one copy, one launch):
     both give the oracle's result, and whole rows agree bit for bit."""
     rng = np.random.default_rng(91 if unit else 92)
-    n, K = 50000, 16
+    n = 50000
     rowoff, col, val = random_csr(rng, n, 200, hubs=3, hub_factor=50)
     if unit:
         val = np.ones_like(val)
@@ -384,8 +384,9 @@ def test_chunked_host_call_matches_single_shot(ctx, oracle, unit):
     origin, srow, scol, sval, cap, tasks = _oracle_pipeline(oracle, rowoff, col, val, costs, 256)
     tk = np.asarray(tasks).reshape(-1, 4)
     order = cs.CSR_Order(srow, scol, sval, origin)
-    chunked, t1 = ctx.spmmKernel(order, H, K, K, tk)
-    single, t2 = ctx.spmmKernel(order, H, K, K, np.ascontiguousarray(tk[::-1]))
+    call = ctx.spmmKernel if K <= 1024 else ctx.spmmKernelLargeKFallback
+    chunked, t1 = call(order, H, K, K, tk)
+    single, t2 = call(order, H, K, K, np.ascontiguousarray(tk[::-1]))
     assert t1 > 0 and t2 > 0
     ref, cond = oracle.spmm_mean_f64(srow, scol, sval, origin, H)
     assert_mean_close(chunked, ref, cond, what="chunked")
