@@ -65,6 +65,8 @@ def parse_args():
                     help="shrink the configuration (profiling captures only; not a bench line)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--deterministic", action="store_true",
+                    help="merge split rows in a fixed order (CWLB_DETERMINISTIC)")
     ap.add_argument("--x-sharded", action="store_true",
                     help="N > 1: X arrives row-sharded (as a prior layer leaves it); every "
                          "step all-gathers it over NCCL before the aggregation")
@@ -278,6 +280,23 @@ class _DevPtr:
                                          "data": (ptr, False), "version": 3}
 
 
+def _scan_launches(n):
+    # device_exclusive_scan: one launch up to 4096 items, else reduce + apply
+    # around a scan of the tile sums.
+    return 1 if n <= 4096 else 2 + _scan_launches(-(-n // 4096))
+
+
+def launches_per_step(flags, n_tasks):
+    """Kernels of this library per aggregation step: the zero pre-pass
+    (rows-covered mode), the aggregation, and in deterministic mode the
+    fragment plan (count, scan, place) and merge (window, final)."""
+    import cwlb_spmm as cs
+    n = 1 + (1 if flags & cs.ROWS_COVERED else 0)
+    if flags & cs.DETERMINISTIC:
+        n += 4 + _scan_launches(n_tasks)
+    return n
+
+
 def run_step(ctx, wl, tasks, n_tasks, out, flags):
     if wl.get("x_sharded"):
         shards.gather_rows(wl["X"], wl["bounds"])
@@ -405,6 +424,7 @@ def run_ours(args):
         tasks, n_tasks, cap, chk = partition(ctx, wl, costs, S)
         flags = cs.ROWS_COVERED if (chk["uncovered_rows"] == 0 and chk["bad_tasks"] == 0 and
                                     chk["nnz_coverage_errors"] == 0) else 0
+        flags |= cs.DETERMINISTIC if args.deterministic else 0
         for _ in range(3):
             run_step(ctx, wl, tasks, n_tasks, out, flags)
         t = allreduce_max(time_steps(ctx, wl, tasks, n_tasks, out, flags, 10) / 10, world)
@@ -422,6 +442,7 @@ def run_ours(args):
     tasks, n_tasks, cap, chk = partition(ctx, wl, costs, S)
     covered = chk["uncovered_rows"] == 0 and chk["bad_tasks"] == 0 and chk["nnz_coverage_errors"] == 0
     flags = cs.ROWS_COVERED if covered else 0
+    flags |= cs.DETERMINISTIC if args.deterministic else 0
 
     for _ in range(args.warmup):
         run_step(ctx, wl, tasks, n_tasks, out, flags)
@@ -498,6 +519,7 @@ def run_ours(args):
                        "n_tasks_rank0": n_tasks, "costs": os.path.relpath(COSTS_FILE, ROOT),
                        "parallelism": f"row shards x{world}" if world > 1 else "single GPU",
                        "ms_per_step_by_rank": per_rank_ms,
+                       "split_row_merge": "deterministic" if args.deterministic else "atomic",
                        "x": ("row-sharded; one NCCL all-gather per step, inside the timing"
                              if wl.get("x_sharded") else "replicated"),
                        "l2": "inputs larger than L2 (CSR + X > 126 MB), no flush",
@@ -517,7 +539,7 @@ def run_ours(args):
                          "gather_tb_s": round(4 * wl["nnz"] * K / per_launch / 1e12, 2),
                          "fma_per_launch": wl["nnz"] * K},
             "e2e": e2e,
-            "gpu_launches": (2 if flags else 1) * args.steps,
+            "gpu_launches": launches_per_step(flags, n_tasks) * args.steps,
             "clocks": clocks,
         }
         if cpu:

@@ -79,6 +79,8 @@ struct cwlb_ctx {
     // 1.0f values for host-buffer calls whose values are all one (not copied).
     cwlb::DeviceBuffer ones;
     size_t ones_count = 0;
+    // Fragment partials and their plan (CWLB_DETERMINISTIC).
+    cwlb::DeviceBuffer det_scratch;
 };
 
 namespace cwlb {

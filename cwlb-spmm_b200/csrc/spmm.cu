@@ -38,6 +38,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "scan.cuh"
 
 namespace cwlb {
 namespace {
@@ -60,6 +61,11 @@ struct SpmmArgs {
     int32_t n_rows;
     int32_t nnz;
     int32_t write_empty;  // rows-covered mode: degree-0 rows get explicit zeros
+    // Deterministic mode: fragments of split rows go to frag (row
+    // frag_pos[2 t + slot] of K floats; slot 0 = the task's first row, 1 = its
+    // last) instead of atomics.  nullptr: atomic mode.
+    float* __restrict__ frag;
+    const int32_t* __restrict__ frag_pos;
 };
 
 __device__ __forceinline__ void raise_err(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
@@ -258,10 +264,19 @@ __device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, 
 template <int V>
 __device__ __forceinline__ void write_row(const SpmmArgs& a, const RowFrag& f,
                                           const int64_t (&q)[V], const bool (&ok)[V],
-                                          float4 (&acc)[V]) {
+                                          float4 (&acc)[V], int64_t t, int slot) {
     float4* out4 = reinterpret_cast<float4*>(a.out) + static_cast<int64_t>(f.orig) * (a.K >> 2);
     const float d = static_cast<float>(f.deg);
     const bool full = f.begin == 0 && f.end == f.deg;
+    if (!full && a.frag != nullptr) {
+        const int32_t pos = __ldg(a.frag_pos + 2 * t + slot);
+        if (pos < 0) return;
+        float4* dst = reinterpret_cast<float4*>(a.frag) + static_cast<int64_t>(pos) * (a.K >> 2);
+#pragma unroll
+        for (int i = 0; i < V; ++i)
+            if (ok[i]) dst[q[i]] = div4(acc[i], d);
+        return;
+    }
 #pragma unroll
     for (int i = 0; i < V; ++i) {
         if (!ok[i]) continue;
@@ -378,7 +393,7 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
                     acc[i].w += __shfl_xor_sync(tmask, acc[i].w, sh);
                 }
             }
-            if (gt == 0) write_row<V>(a, f, q, ok, acc);
+            if (gt == 0) write_row<V>(a, f, q, ok, acc, t, r == tk.row_start ? 0 : 1);
         }
     } else {
         // One row: the G groups take interleaved chunks, then reduce by
@@ -405,7 +420,7 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
                 acc[i].w += __shfl_xor_sync(0xffffffffu, acc[i].w, s);
             }
         }
-        if (g == 0) write_row<V>(a, f, q, ok, acc);
+        if (g == 0) write_row<V>(a, f, q, ok, acc, t, 0);
     }
 }
 
@@ -459,11 +474,18 @@ __global__ void __launch_bounds__(kThreads) spmm_scalar_kernel(SpmmArgs a) {
         }
         const float d = static_cast<float>(f.deg);
         const bool full = f.begin == 0 && f.end == f.deg;
+        float* frow = nullptr;  // deterministic mode: this fragment's scratch row
+        if (!full && a.frag != nullptr) {
+            const int32_t pos = __ldg(a.frag_pos + 2 * t + (r == tk.row_start ? 0 : 1));
+            if (pos < 0) continue;
+            frow = a.frag + static_cast<int64_t>(pos) * a.K;
+        }
 #pragma unroll
         for (int i = 0; i < V; ++i) {
             if (!ok[i]) continue;
             const float r_ = __fdiv_rn(acc[i], d);
             if (full) __stcs(orow + kk[i], r_);
+            else if (frow) frow[kk[i]] = r_;
             else atomicAdd(orow + kk[i], r_);
         }
     }
@@ -523,6 +545,126 @@ __global__ void __launch_bounds__(kThreads) zero_split_rows_kernel(SpmmArgs a) {
                 for (int64_t k = lane; k < a.K; k += 32) row[k] = 0.0f;
             }
         }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Deterministic merge of split rows (CWLB_DETERMINISTIC).
+//
+// Only a task's first and last rows can be partial.  Plan: count each task's
+// partial rows (0-2), scan the counts into positions, and record each
+// fragment's row in task order; a row split by the partitioner lies in
+// consecutive tasks, so its fragments are consecutive.  The aggregation stores
+// every fragment's partial mean at its position.  Then each window of 64
+// consecutive fragments is summed per row in order, in place at the first
+// fragment of each row's piece, and one warp per row adds its pieces in order
+// into the zeroed output row.
+
+constexpr int kMergeWindow = 64;
+
+// Bit 0: the task's first row is partial; bit 1: its (different) last row.
+// Mirrors row_fragment: rows with bad offsets or origins are never written.
+__device__ __forceinline__ int task_partial_rows(const SpmmArgs& a, const cwlb_task& tk) {
+    if (tk.row_start < 0 || tk.row_end > a.n_rows || tk.row_start >= tk.row_end) return 0;
+    int m = 0;
+    for (int s = 0; s < 2; ++s) {
+        const int r = s == 0 ? tk.row_start : tk.row_end - 1;
+        if (s == 1 && r == tk.row_start) break;
+        const int32_t b0 = __ldg(a.rowoff + r), b1 = __ldg(a.rowoff + r + 1);
+        if (b0 < 0 || b1 < b0 || b1 > a.nnz) continue;
+        const int32_t o = __ldg(a.origin + r);
+        if (o < 0 || o >= a.n_rows) continue;
+        const int32_t deg = b1 - b0;
+        if (deg <= 0) continue;
+        int32_t begin = (r == tk.row_start) ? tk.first_row_offset : 0;
+        int32_t end = deg;
+        if (r == tk.row_end - 1 && tk.last_row_nnz > 0) end = tk.last_row_nnz;
+        begin = min(max(begin, 0), deg);
+        end = min(max(end, begin), deg);
+        if (begin < end && !(begin == 0 && end == deg)) m |= 1 << s;
+    }
+    return m;
+}
+
+__device__ __forceinline__ cwlb_task load_task_raw(const SpmmArgs& a, int64_t t) {
+    return cwlb_task{__ldg(&a.tasks[t].row_start), __ldg(&a.tasks[t].row_end),
+                     __ldg(&a.tasks[t].first_row_offset), __ldg(&a.tasks[t].last_row_nnz)};
+}
+
+__global__ void __launch_bounds__(kThreads) frag_count_kernel(SpmmArgs a, int32_t* cnt) {
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    if (t >= a.n_tasks) return;
+    cnt[t] = __popc(task_partial_rows(a, load_task_raw(a, t)));
+}
+
+__global__ void __launch_bounds__(kThreads)
+    frag_place_kernel(SpmmArgs a, const int32_t* __restrict__ cnt, const int32_t* __restrict__ base,
+                      int32_t* __restrict__ frag_pos, int32_t* __restrict__ entry_row,
+                      int32_t* __restrict__ n_frag) {
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    if (t >= a.n_tasks) return;
+    const cwlb_task tk = load_task_raw(a, t);
+    const int m = task_partial_rows(a, tk);
+    int32_t p = base[t];
+    frag_pos[2 * t] = (m & 1) ? p : -1;
+    if (m & 1) entry_row[p++] = tk.row_start;
+    frag_pos[2 * t + 1] = (m & 2) ? p : -1;
+    if (m & 2) entry_row[p++] = tk.row_end - 1;
+    if (t == a.n_tasks - 1) *n_frag = base[t] + cnt[t];
+}
+
+// Warp w sums fragments [64 w, 64 w + 64) per row piece, in order, and leaves
+// each piece's sum at the piece's first fragment.
+__global__ void __launch_bounds__(kThreads)
+    frag_window_kernel(float* __restrict__ frag, const int32_t* __restrict__ entry_row,
+                       const int32_t* __restrict__ n_frag, int64_t K) {
+    const int64_t w = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t nf = *n_frag;
+    const int64_t i0 = w * kMergeWindow;
+    if (i0 >= nf) return;
+    const int64_t i1 = min(i0 + kMergeWindow, nf);
+    for (int64_t k = lane; k < K; k += 32) {
+        int64_t start = i0;
+        int32_t row = entry_row[i0];
+        float sum = frag[i0 * K + k];
+        for (int64_t i = i0 + 1; i < i1; ++i) {
+            const int32_t ri = entry_row[i];
+            const float v = frag[i * K + k];
+            if (ri != row) {
+                frag[start * K + k] = sum;
+                start = i;
+                row = ri;
+                sum = v;
+            } else {
+                sum += v;
+            }
+        }
+        frag[start * K + k] = sum;
+    }
+}
+
+// One warp per row's first fragment: its pieces (the first, then one per
+// window boundary inside the row's fragment run) added in order.
+__global__ void __launch_bounds__(kThreads)
+    frag_final_kernel(const float* __restrict__ frag, const int32_t* __restrict__ entry_row,
+                      const int32_t* __restrict__ n_frag, const int32_t* __restrict__ origin,
+                      int64_t K, int64_t max_frag, float* __restrict__ out) {
+    const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (i >= max_frag) return;
+    const int64_t nf = *n_frag;
+    if (i >= nf) return;
+    const int32_t R = entry_row[i];
+    if (i > 0 && entry_row[i - 1] == R) return;
+    const int32_t o = __ldg(origin + R);  // checked by the plan
+    for (int64_t k = lane; k < K; k += 32) {
+        float sum = frag[i * K + k];
+        for (int64_t p = (i / kMergeWindow + 1) * kMergeWindow; p < nf && entry_row[p] == R;
+             p += kMergeWindow)
+            sum += frag[p * K + k];
+        // Added onto the zeroed row: exact for a row with one fragment run.
+        atomicAdd(out + static_cast<int64_t>(o) * K + k, sum);
     }
 }
 
@@ -616,6 +758,40 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
         CWLB_LAUNCH_CHECK("zero_split_rows_kernel");
     }
 
+    // Deterministic mode: plan the fragment positions (scratch carved from
+    // one context buffer, every piece 256-byte aligned).
+    const bool det = (flags & CWLB_DETERMINISTIC) != 0;
+    int32_t* n_frag = nullptr;
+    int32_t* entry_row = nullptr;
+    const int64_t max_frag = 2 * n_tasks;
+    if (det) {
+        if (max_frag >= (int64_t(1) << 31)) {
+            fail(CWLB_ERR_INVALID_ARGUMENT, "deterministic mode supports fewer than 2^30 tasks");
+        }
+        auto al = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
+        const size_t nt = static_cast<size_t>(n_tasks), mf = static_cast<size_t>(max_frag);
+        const size_t b_cnt = al(4 * nt), b_scan = al(scan_scratch_bytes<int32_t>(n_tasks));
+        const size_t b_pos = al(4 * mf), b_nf = 256;
+        const size_t b_frag = al(sizeof(float) * mf * static_cast<size_t>(K));
+        char* base = static_cast<char*>(
+            ctx->det_scratch.ensure(2 * b_cnt + b_scan + 2 * b_pos + b_nf + b_frag));
+        int32_t* cnt = reinterpret_cast<int32_t*>(base);
+        int32_t* offs = reinterpret_cast<int32_t*>(base + b_cnt);
+        void* scan_tmp = base + 2 * b_cnt;
+        int32_t* frag_pos = reinterpret_cast<int32_t*>(base + 2 * b_cnt + b_scan);
+        entry_row = reinterpret_cast<int32_t*>(base + 2 * b_cnt + b_scan + b_pos);
+        n_frag = reinterpret_cast<int32_t*>(base + 2 * b_cnt + b_scan + 2 * b_pos);
+        float* frag = reinterpret_cast<float*>(base + 2 * b_cnt + b_scan + 2 * b_pos + b_nf);
+        const unsigned g = static_cast<unsigned>(ceil_div(n_tasks, kThreads));
+        frag_count_kernel<<<g, kThreads, 0, s>>>(a, cnt);
+        CWLB_LAUNCH_CHECK("frag_count_kernel");
+        device_exclusive_scan<int32_t>(cnt, offs, n_tasks, scan_tmp, s);
+        frag_place_kernel<<<g, kThreads, 0, s>>>(a, cnt, offs, frag_pos, entry_row, n_frag);
+        CWLB_LAUNCH_CHECK("frag_place_kernel");
+        a.frag = frag;
+        a.frag_pos = frag_pos;
+    }
+
     const bool aligned = (reinterpret_cast<uintptr_t>(H) % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(out) % 16 == 0) && (K % 4 == 0);
     if (aligned) {
@@ -647,6 +823,16 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
             default: spmm_scalar_kernel<4><<<grid, kThreads, 0, s>>>(a); break;
         }
         CWLB_LAUNCH_CHECK("spmm_scalar_kernel");
+    }
+    if (det) {
+        const unsigned gw = static_cast<unsigned>(
+            std::max<int64_t>(1, ceil_div(ceil_div(max_frag, kMergeWindow), kWarpsPerCta)));
+        frag_window_kernel<<<gw, kThreads, 0, s>>>(a.frag, entry_row, n_frag, K);
+        CWLB_LAUNCH_CHECK("frag_window_kernel");
+        const unsigned gf = static_cast<unsigned>(ceil_div(max_frag, kWarpsPerCta));
+        frag_final_kernel<<<gf, kThreads, 0, s>>>(a.frag, entry_row, n_frag, origin, K, max_frag,
+                                                  out);
+        CWLB_LAUNCH_CHECK("frag_final_kernel");
     }
 }
 

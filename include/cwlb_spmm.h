@@ -135,8 +135,14 @@ int cwlb_spmm_kernel_large_k(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
  * flags: 0 -> out is zero-filled first (reference semantics);
  * CWLB_ROWS_COVERED -> the caller asserts that the tasks cover every row
  * (see cwlb_tasks_check); the kernels then write every output row themselves
- * and the full zero-fill is skipped. */
+ * and the full zero-fill is skipped.
+ * CWLB_DETERMINISTIC -> rows split across tasks are merged in a fixed order
+ * (fragment partials kept in context scratch of up to 2 x n_tasks x K floats,
+ * then summed per row in task order, in blocks of 64 fragments) instead of
+ * with float atomics, so repeated calls give bit-identical outputs; the
+ * reference's atomics (src/parallelMatrix.cpp:219-234) promise no order. */
 #define CWLB_ROWS_COVERED 1u
+#define CWLB_DETERMINISTIC 2u
 int cwlb_spmm_mean_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
                           const int32_t* d_row_offset, const int32_t* d_col_ind,
                           const float* d_value, const int32_t* d_origin_local, const float* d_H,

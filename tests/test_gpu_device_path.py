@@ -204,3 +204,55 @@ def test_reference_kernel_flags_bad_columns(ctx):
     assert ctx.take_device_errors() == cs.DEVERR_COL_RANGE
     # The bad entry is skipped; the mean still divides by the stored degree.
     assert torch.equal(out.cpu(), torch.tensor([[0., 0.5, 1., 1.5], [4., 5., 6., 7.]]))
+
+
+@pytest.mark.parametrize("K,S,covered", [(7, 16, False), (32, 16, True), (128, 9, True),
+                                         (512, 64, False), (1100, 32, True)])
+def test_deterministic_mode_is_reproducible(ctx, oracle, K, S, covered):
+    """CWLB_DETERMINISTIC merges split rows in task order: two runs give the
+    same bits, the result is within the tolerance of the exact mean, and rows
+    that are never split equal the atomic mode's."""
+    rng = np.random.default_rng(300 + K)
+    from helpers import random_csr
+    rowoff, col, val = random_csr(rng, 4000, 80, n_cols=3000, hubs=4, hub_factor=60)
+    X = rng.standard_normal((3000, K)).astype(np.float32)
+    costs = cs.SpmmCostParams(0.02, 0.7, 0.3, 0.5)
+    p = _device_pipeline(ctx, rowoff, col, val, X, costs, S)
+    n = p["n"]
+    flags = cs.DETERMINISTIC | (cs.ROWS_COVERED if covered else 0)
+    outs = []
+    for f in (flags, flags, cs.ROWS_COVERED if covered else 0):
+        out = torch.full((n, K), float("nan"), device="cuda:0")
+        if not covered:
+            out.zero_()
+        ctx.spmm_mean_device(n, p["nnz"], p["sro"].data_ptr(), p["scol"].data_ptr(),
+                             p["sval"].data_ptr(), p["org"].data_ptr(), p["X"].data_ptr(), 3000, K,
+                             p["t_ptr"], p["n_tasks"], out.data_ptr(), f)
+        torch.cuda.synchronize()
+        assert ctx.take_device_errors() == 0
+        outs.append(out.cpu().numpy())
+    det1, det2, atomic = outs
+    assert np.array_equal(det1, det2)
+    o = oracle.sort_by_degree(rowoff, col, val)
+    ref, cond = oracle.spmm_mean_f64(o[1], o[2], o[3], o[0], X)
+    assert_mean_close(det1, ref, cond, what=f"deterministic K={K}")
+    tasks = torch.as_tensor(_DevTasks(p["t_ptr"], p["n_tasks"]), device="cuda:0").cpu().numpy()
+    tasks = tasks.reshape(-1, 4)
+    deg = np.diff(o[1])
+    split = set()
+    for rs, re_, fo, ln in tasks:
+        for r in (rs, re_ - 1):
+            b = fo if r == rs else 0
+            e = ln if (r == re_ - 1 and ln > 0) else deg[r]
+            if deg[r] > 0 and b < e and not (b == 0 and e == deg[r]):
+                split.add(int(r))
+    assert split, "the case must split rows"
+    keep = np.ones(n, bool)
+    keep[o[0][sorted(split)]] = False
+    assert np.array_equal(det1[keep], atomic[keep])
+
+
+class _DevTasks:
+    def __init__(self, ptr, count):
+        self.__cuda_array_interface__ = {"shape": (count * 4,), "typestr": "<i4",
+                                         "data": (ptr, False), "version": 3}
