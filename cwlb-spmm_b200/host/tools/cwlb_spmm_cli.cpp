@@ -11,7 +11,8 @@
 // CWLB_DATASET_DIR, CWLB_COSTFILE and CWLB_RESULTS; CWLB_DEVICE picks the GPU.
 //
 // Extensions: CWLB_CSR_CACHE=1 loads the dataset through the binary cache
-// beside the text file (data.h), and a trailing --verify checks every run's output with
+// beside the text file (data.h), CWLB_DETERMINISTIC=1 merges split rows in a
+// fixed order (bit-reproducible outputs), and a trailing --verify checks every run's output with
 // validate_custom_csr_result (absolute tolerance 1e-4) against a float64
 // aggregation of the UNSORTED CSR computed on the device
 // (cwlb_spmm_mean_reference_device), and exits with status 1 on a mismatch.
@@ -205,7 +206,9 @@ public:
         cwlb::check(cwlb_tasks_check(q_.ctx(), n, nnz, ro_.p,
                                      reinterpret_cast<const cwlb_task*>(d_tasks.p),
                                      static_cast<int64_t>(tasks.size()), &bad, &unc, &cov));
-        const uint32_t flags = (bad == 0 && unc == 0 && cov == 0) ? CWLB_ROWS_COVERED : 0u;
+        uint32_t flags = (bad == 0 && unc == 0 && cov == 0) ? CWLB_ROWS_COVERED : 0u;
+        const char* det = std::getenv("CWLB_DETERMINISTIC");
+        if (det && std::string(det) == "1") flags |= CWLB_DETERMINISTIC;
         cudaStream_t st = static_cast<cudaStream_t>(cwlb_ctx_stream(q_.ctx()));
         double sum = 0.0;
         for (int it = 0; it < LOOPCOUNT; ++it) {

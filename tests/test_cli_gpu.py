@@ -173,6 +173,15 @@ def test_cli_csr_cache(workdir):
     assert "V: 512, E: " in outs[1] and "Validation passed" in outs[1]
 
 
+def test_cli_deterministic_mode_verifies(workdir):
+    env = _env()
+    env["CWLB_DETERMINISTIC"] = "1"
+    p = subprocess.run([CWLB, "g", "16", "--S", "2", "--verify"], cwd=workdir / "build",
+                       capture_output=True, text=True, env=env, timeout=900)
+    assert p.returncode == 0, p.stderr
+    assert "Validation passed" in p.stdout
+
+
 def test_costwrite_writes_cost_file(workdir):
     rc, out, err = run([COSTWRITE, "32", "5", "8192", "16", "4"], workdir / "build")
     assert rc == 0, err
