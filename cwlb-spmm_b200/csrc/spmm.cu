@@ -183,23 +183,56 @@ struct VecCfg {
 // (each at most L long, ending at `end`) into acc.  All lanes of the group
 // execute this with the same arguments.  Per column, the FMA chain follows
 // increasing nonzero index within each chunk and chunk order.
-template <int L, int V>
+//
+// kPrefetch: the next chunk's pair is loaded before this chunk's gathers, so
+// its latency overlaps them (6% on configuration 5, 1.5% on 2).  Used by the
+// <16,1>, <16,2> and <32,1> shapes outside short-row mode; short-row mode was
+// 10% slower with it (configuration 4), and wider or narrower shapes gain
+// registers and lose an occupancy step.
+template <int L, int V, bool kPrefetch>
 __device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, int32_t end,
                                               int32_t step, unsigned gmask, int lg,
                                               const float4* const (&hq)[V], const bool (&ok)[V],
                                               uint32_t K4, float4 (&acc)[V]) {
     constexpr int U = VecCfg<L, V>::U;
+    [[maybe_unused]] int32_t nc = 0;
+    [[maybe_unused]] float nv = 0.0f;
+    if constexpr (kPrefetch) {
+        if (start < end && lg < min(L, end - start)) {
+            nc = __ldg(a.col + start + lg);
+            nv = __ldg(a.val + start + lg);
+        }
+    }
     for (int32_t pos = start; pos < end; pos += step) {
         const int32_t cnt = min(L, end - pos);
         int32_t c = 0;
         float v = 0.0f;
-        if (lg < cnt) {
-            c = __ldg(a.col + pos + lg);
-            v = __ldg(a.val + pos + lg);
-            if (static_cast<uint32_t>(c) >= static_cast<uint64_t>(a.h_rows)) {
+        if constexpr (kPrefetch) {
+            if (lg < cnt) {
+                c = nc;
+                v = nv;
+            }
+            const int32_t np = pos + step;
+            nc = 0;
+            nv = 0.0f;
+            if (np < end && lg < min(L, end - np)) {
+                nc = __ldg(a.col + np + lg);
+                nv = __ldg(a.val + np + lg);
+            }
+            if (lg < cnt && static_cast<uint32_t>(c) >= static_cast<uint64_t>(a.h_rows)) {
                 raise_err(a.err, CWLB_DEVERR_COL_RANGE);
                 c = 0;
                 v = 0.0f;
+            }
+        } else {
+            if (lg < cnt) {
+                c = __ldg(a.col + pos + lg);
+                v = __ldg(a.val + pos + lg);
+                if (static_cast<uint32_t>(c) >= static_cast<uint64_t>(a.h_rows)) {
+                    raise_err(a.err, CWLB_DEVERR_COL_RANGE);
+                    c = 0;
+                    v = 0.0f;
+                }
             }
         }
         if (cnt == L) {
@@ -382,7 +415,7 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
             float4 acc[V];
 #pragma unroll
             for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            gather_chunks<L, V>(a, f.base + f.begin + gt * L, f.base + f.end, team_lanes, gmask, lg,
+            gather_chunks<L, V, !kStage && L >= 16 && L * V <= 32>(a, f.base + f.begin + gt * L, f.base + f.end, team_lanes, gmask, lg,
                                 hq, ok, K4, acc);
             for (int sh = L; sh < team_lanes; sh <<= 1) {
 #pragma unroll
@@ -408,7 +441,7 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
         float4 acc[V];
 #pragma unroll
         for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        gather_chunks<L, V>(a, f.base + f.begin + g * L, f.base + f.end, 32, gmask, lg, hq, ok,
+        gather_chunks<L, V, !kStage && L >= 16 && L * V <= 32>(a, f.base + f.begin + g * L, f.base + f.end, 32, gmask, lg, hq, ok,
                             K4, acc);
 #pragma unroll
         for (int s = L; s < 32; s <<= 1) {
