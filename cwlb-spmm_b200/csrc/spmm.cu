@@ -661,16 +661,26 @@ __global__ void __launch_bounds__(kThreads)
         int64_t start = i0;
         int32_t row = entry_row[i0];
         float sum = frag[i0 * K + k];
-        for (int64_t i = i0 + 1; i < i1; ++i) {
-            const int32_t ri = entry_row[i];
-            const float v = frag[i * K + k];
-            if (ri != row) {
-                frag[start * K + k] = sum;
-                start = i;
-                row = ri;
-                sum = v;
-            } else {
-                sum += v;
+        // Entries read 8 at a time (loads in flight together), summed in order.
+        for (int64_t i = i0 + 1; i < i1; i += 8) {
+            float v[8];
+            int32_t rr[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                rr[u] = (i + u < i1) ? entry_row[i + u] : -1;
+                v[u] = (i + u < i1) ? frag[(i + u) * K + k] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (i + u >= i1) break;
+                if (rr[u] != row) {
+                    frag[start * K + k] = sum;
+                    start = i + u;
+                    row = rr[u];
+                    sum = v[u];
+                } else {
+                    sum += v[u];
+                }
             }
         }
         frag[start * K + k] = sum;
@@ -691,11 +701,23 @@ __global__ void __launch_bounds__(kThreads)
     const int32_t R = entry_row[i];
     if (i > 0 && entry_row[i - 1] == R) return;
     const int32_t o = __ldg(origin + R);  // checked by the plan
+    // The row's pieces: its first fragment, then every window boundary inside
+    // its run.  Counted once, then read 8 at a time (loads in flight together)
+    // and added strictly in order.
+    const int64_t p0 = (i / kMergeWindow + 1) * kMergeWindow;
+    int64_t n_more = 0;
+    while (p0 + n_more * kMergeWindow < nf && entry_row[p0 + n_more * kMergeWindow] == R) ++n_more;
     for (int64_t k = lane; k < K; k += 32) {
         float sum = frag[i * K + k];
-        for (int64_t p = (i / kMergeWindow + 1) * kMergeWindow; p < nf && entry_row[p] == R;
-             p += kMergeWindow)
-            sum += frag[p * K + k];
+        for (int64_t j = 0; j < n_more; j += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                v[u] = (j + u < n_more) ? frag[(p0 + (j + u) * kMergeWindow) * K + k] : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (j + u < n_more) sum += v[u];
+        }
         // Added onto the zeroed row: exact for a row with one fragment run.
         atomicAdd(out + static_cast<int64_t>(o) * K + k, sum);
     }
