@@ -44,6 +44,12 @@ struct ErrorElement {
 // the reference's sortCSRByDegreeDPLCPU (main.cpp:197-278), on the GPU.
 CSR_Order sortCSRByDegree(const CSR& csr, cwlb::Queue& q);
 
+// sortCSRByDegree_SYCL (include/utils.h:13, src/utils.cpp:104-339): the
+// reference's optional GPU bucket ordering, whose ties come out in any order.
+// Here the same device sort as above: ascending degree, ties by original id
+// (one of the orders the bucket sort may produce).
+CSR_Order sortCSRByDegree_SYCL(const CSR& csr, cwlb::Queue& q);
+
 // measure_spmm_costs (utils.h:47-54): the four calibration microbenchmarks.
 SpmmCostParams measure_spmm_costs(cwlb::Queue& q, int K = 128, int repeat = 500,
                                   int WI = 131072, int data_MB_for_load = 512,

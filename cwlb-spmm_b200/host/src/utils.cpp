@@ -66,6 +66,8 @@ CSR_Order sortCSRByDegree(const CSR& csr, cwlb::Queue& q) {
     return out;
 }
 
+CSR_Order sortCSRByDegree_SYCL(const CSR& csr, cwlb::Queue& q) { return sortCSRByDegree(csr, q); }
+
 SpmmCostParams measure_spmm_costs(cwlb::Queue& q, int K, int repeat, int WI, int data_MB_for_load,
                                   int atomic_target_writers, const std::vector<int>&) {
     cwlb_costs c{};
