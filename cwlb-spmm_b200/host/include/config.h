@@ -3,12 +3,15 @@
 // C++ interface (reference: include/config.h:1-25), for the B200 build.
 //
 // The paths keep the reference's defaults (relative to a build/ working
-// directory); the CWLB_COSTFILE, CWLB_DATASET_DIR and CWLB_RESULTS environment
-// variables override them (see cwlb_paths.h).
+// directory); the dataset loader honours CWLB_DATASET_DIR, and the cwlb-spmm
+// tool CWLB_COSTFILE and CWLB_RESULTS.
 #include <cstddef>
 #include <stdexcept>
 #include <string>
 #include <vector>
+
+// As in the reference's config.h: code written against it may rely on this.
+using namespace std;
 
 // Timed samples = LOOPCOUNT - WARMUPCOUNT; LOOPCOUNT includes the warm-up.
 inline const int WARMUPCOUNT = 20;
