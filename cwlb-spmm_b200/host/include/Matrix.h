@@ -1,5 +1,12 @@
 #pragma once
 // CSR storage of the CWLB-SpMM interface (reference: include/Matrix.h:15-36).
+// The standard headers the reference's Matrix.h brings in are included too,
+// since code written against it may use them through this header.
+#include <fstream>
+#include <iostream>
+#include <map>
+#include <sstream>
+#include <string>
 #include <vector>
 
 #include "config.h"
