@@ -188,3 +188,51 @@ def test_costwrite_argument_errors(workdir, argv):
         assert err.strip() == "stoi"
     else:
         assert err.strip() == "All microbenchmark parameters must be positive."
+
+
+def _big_text(rng, n, nnz):
+    deg = rng.multinomial(nnz, np.ones(n) / n)
+    ro = np.zeros(n + 1, np.int64)
+    np.cumsum(deg, out=ro[1:])
+    col = rng.integers(0, n, nnz)
+    return ro, col
+
+
+@pytest.mark.parametrize("damage", [None, "late_letter", "early_overflow", "mid_space"])
+def test_loader_parallel_parse_matches_reference(workdir, reference, damage):
+    """Lines long enough for the multi-threaded parse (2M column ids, ~16 MB):
+    the same arrays as the reference's loader, or the same error."""
+    rng = np.random.default_rng(3)
+    ro, col = _big_text(rng, 100_000, 2_000_000)
+    cells = [str(x) for x in col.tolist()]
+    if damage == "late_letter":
+        cells[-5] = "x7"
+    elif damage == "early_overflow":
+        cells[1000] = "99999999999"
+        cells[-10] = "y"
+    elif damage == "mid_space":
+        cells[len(cells) // 2] = " "
+    text = ",".join(map(str, ro.tolist())) + "\n" + ",".join(cells) + "\n"
+    write_ds(workdir, "big", text)
+    path = str(workdir / "resources" / "datasets" / "big.csr")
+    rc, out, err = run([CSRCHECK, path], workdir / "build")
+    cwd = os.getcwd()
+    os.chdir(workdir / "build")
+    try:
+        if damage is None:
+            rro, rcol, _, V, E = reference.load_csr("big")
+        else:
+            with pytest.raises(Exception) as ei:
+                reference.load_csr("big")
+    finally:
+        os.chdir(cwd)
+    if damage is None:
+        assert rc == 0, err
+        assert out.split()[:2] == [str(V), str(E)]
+        h = 1469598103934665603
+        for v in np.concatenate([rro, rcol]).astype(np.uint32).tolist():
+            for i in range(4):
+                h = ((h ^ ((v >> (8 * i)) & 0xFF)) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+        assert out.split()[2] == f"{h:016x}"
+    else:
+        assert rc == 1 and err.strip() == str(ei.value)
