@@ -8,13 +8,17 @@
 //   2. LSD radix sort, 8 bits per pass, as many passes as the largest degree
 //      needs.  Each pass: per-tile digit histograms, one exclusive scan over
 //      the digit-major histogram table, then a stable scatter in which every
-//      tile ranks its items with warp match/ballot and per-warp digit counts;
+//      tile ranks its items with warp match/ballot and per-warp digit counts.
+//      A tile is 256 x R items, R in [1, 16] chosen so that a pass has about
+//      two tiles per SM (short row arrays would otherwise run on a few CTAs);
 //   3. new offsets = exclusive scan of the sorted degrees (int32, since
 //      nnz < 2^31 is a precondition of the int32 CSR);
 //   4. rows are gathered by output position: each CTA owns 2048 consecutive
-//      output nonzeros, stages the offsets of the (at most 2048) rows they
-//      span in shared memory and binary-searches there, so hub rows are split
-//      across CTAs and stores are coalesced.
+//      output nonzeros.  A kernel over rows first records, per chunk, the rows
+//      holding its first and last position; the CTA stages the offsets of the
+//      (at most 2048) rows in between in shared memory and binary-searches
+//      there, so hub rows are split across CTAs and stores are coalesced.  All
+//      of a thread's loads are issued before its stores.
 // The reference's own GPU sorter (src/utils.cpp:106-339) uses an atomic
 // bucket scatter whose tie order is nondeterministic; it is not the parity
 // target.
@@ -25,8 +29,7 @@ namespace cwlb {
 namespace {
 
 constexpr int kSortThreads = 256;
-constexpr int kSortRounds = 16;
-constexpr int kSortTile = kSortThreads * kSortRounds;  // 4096 items per tile
+constexpr int kSortMaxRounds = 16;  // tile = kSortThreads x rounds items
 constexpr int kRadix = 256;
 
 __global__ void degrees_kernel(const int32_t* __restrict__ rowoff, int32_t n, int32_t nnz,
@@ -47,14 +50,14 @@ __global__ void degrees_kernel(const int32_t* __restrict__ rowoff, int32_t n, in
 }
 
 __global__ void __launch_bounds__(kSortThreads)
-    radix_hist_kernel(const uint32_t* __restrict__ keys, int32_t n, int shift, int64_t n_tiles,
-                      int32_t* __restrict__ hist) {
+    radix_hist_kernel(const uint32_t* __restrict__ keys, int32_t n, int shift, int rounds,
+                      int64_t n_tiles, int32_t* __restrict__ hist) {
     __shared__ int32_t h[kRadix];
     h[threadIdx.x] = 0;
     __syncthreads();
-    const int64_t base = static_cast<int64_t>(blockIdx.x) * kSortTile;
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * kSortThreads * rounds;
 #pragma unroll 4
-    for (int r = 0; r < kSortRounds; ++r) {
+    for (int r = 0; r < rounds; ++r) {
         const int64_t i = base + r * kSortThreads + threadIdx.x;
         if (i < n) atomicAdd(&h[(keys[i] >> shift) & 0xffu], 1);
     }
@@ -64,7 +67,7 @@ __global__ void __launch_bounds__(kSortThreads)
 
 __global__ void __launch_bounds__(kSortThreads)
     radix_scatter_kernel(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_in,
-                         int32_t n, int shift, int64_t n_tiles,
+                         int32_t n, int shift, int rounds, int64_t n_tiles,
                          const int32_t* __restrict__ offsets, uint32_t* __restrict__ keys_out,
                          int32_t* __restrict__ vals_out) {
     constexpr int kWarps = kSortThreads / 32;
@@ -76,8 +79,8 @@ __global__ void __launch_bounds__(kSortThreads)
     if (threadIdx.x < kWarps) wcount[threadIdx.x][kRadix] = 0;
     __syncthreads();
     const unsigned lt_mask = (1u << lane) - 1u;
-    const int64_t base = static_cast<int64_t>(blockIdx.x) * kSortTile;
-    for (int r = 0; r < kSortRounds; ++r) {
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * kSortThreads * rounds;
+    for (int r = 0; r < rounds; ++r) {
         const int64_t i = base + r * kSortThreads + threadIdx.x;
         const bool valid = i < n;
         uint32_t key = 0;
@@ -123,44 +126,83 @@ __device__ __forceinline__ int32_t upper_bound_i32(const int32_t* a, int32_t n, 
     return lo;
 }
 
+// Rows holding the first and the last position of every output chunk:
+// first_row[m] is the row containing m*kGatherChunk, last_row[m] the row
+// containing min((m+1)*kGatherChunk, nnz) - 1.  One thread per row writes the
+// entries of the chunk boundaries that fall inside it; entries nobody writes
+// keep the -1 they were cleared to (only with corrupt offsets).
+__global__ void chunk_rows_kernel(const int32_t* __restrict__ new_rowoff, int32_t n, int32_t nnz,
+                                  int32_t* __restrict__ first_row, int32_t* __restrict__ last_row,
+                                  uint32_t* err) {
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (r >= n) return;
+    const int32_t a = new_rowoff[r], b = new_rowoff[r + 1];
+    if (a < 0 || b < a || b > nnz) {
+        atomicOr(err, CWLB_DEVERR_OFFSETS);
+        return;
+    }
+    if (a == b) return;
+    constexpr int64_t C = kGatherChunk;
+    const int64_t n_chunks = (static_cast<int64_t>(nnz) + C - 1) / C;
+    // Chunk starts m*C in [a, b).
+    for (int64_t m = (a + C - 1) / C; m * C < b; ++m) first_row[m] = static_cast<int32_t>(r);
+    // Chunk ends (m+1)*C - 1 in [a, b), i.e. (m+1)*C in [a+1, b].
+    for (int64_t m1 = (a + C) / C; m1 * C <= b; ++m1)
+        last_row[m1 - 1] = static_cast<int32_t>(r);
+    if (b == nnz) last_row[n_chunks - 1] = static_cast<int32_t>(r);  // ragged last chunk
+}
+
 __global__ void __launch_bounds__(kGatherThreads)
     gather_rows_kernel(const int32_t* __restrict__ rowoff, const int32_t* __restrict__ col,
                        const float* __restrict__ val, const int32_t* __restrict__ origin,
-                       const int32_t* __restrict__ new_rowoff, int32_t n, int32_t nnz,
+                       const int32_t* __restrict__ new_rowoff, const int32_t* __restrict__ first_row,
+                       const int32_t* __restrict__ last_row, int32_t n, int32_t nnz,
                        int32_t* __restrict__ new_col, float* __restrict__ new_val, uint32_t* err) {
     __shared__ int32_t s_off[kGatherChunk + 1];  // new offsets of the spanned rows
     __shared__ int32_t s_src[kGatherChunk];      // their source offsets
-    __shared__ int32_t s_rows[2];
     const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kGatherChunk;
     const int32_t c1 = static_cast<int32_t>(min(c0 + kGatherChunk, static_cast<int64_t>(nnz)));
-    if (threadIdx.x == 0) {
-        // Rows containing the first and last position (empty rows skipped:
-        // upper_bound lands on the last row starting at or before p).
-        s_rows[0] = upper_bound_i32(new_rowoff, n + 1, static_cast<int32_t>(c0)) - 1;
-        s_rows[1] = upper_bound_i32(new_rowoff, n + 1, c1 - 1) - 1;
-    }
-    __syncthreads();
-    const int32_t r0 = s_rows[0];
-    const int32_t nr = s_rows[1] - r0 + 1;  // <= kGatherChunk: these rows are non-empty
-    if (nr < 1 || nr > kGatherChunk) {
+    const int32_t r0 = first_row[blockIdx.x];
+    const int32_t r1 = last_row[blockIdx.x];
+    // Uniform over the CTA: every thread leaves here or none does.
+    if (r0 < 0 || r1 < r0 || r1 >= n || r1 - r0 + 1 > kGatherChunk) {
         if (threadIdx.x == 0) atomicOr(err, CWLB_DEVERR_OFFSETS);
         return;
     }
+    const int32_t nr = r1 - r0 + 1;
     for (int k = threadIdx.x; k <= nr; k += kGatherThreads) s_off[k] = new_rowoff[r0 + k];
     for (int k = threadIdx.x; k < nr; k += kGatherThreads) s_src[k] = rowoff[origin[r0 + k]];
     __syncthreads();
+    int32_t src[kGatherItems];
 #pragma unroll
     for (int e = 0; e < kGatherItems; ++e) {
         const int32_t p = static_cast<int32_t>(c0) + e * kGatherThreads + threadIdx.x;
-        if (p >= c1) break;
-        const int32_t k = upper_bound_i32(s_off, nr + 1, p) - 1;
-        const int32_t src = (k >= 0 && k < nr) ? s_src[k] + (p - s_off[k]) : -1;
-        if (src < 0 || src >= nnz) {  // only reachable with corrupt offsets
-            atomicOr(err, CWLB_DEVERR_OFFSETS);
-            continue;
+        src[e] = -1;
+        if (p < c1) {
+            const int32_t k = upper_bound_i32(s_off, nr + 1, p) - 1;
+            src[e] = (k >= 0 && k < nr) ? s_src[k] + (p - s_off[k]) : -1;
+            if (src[e] < 0 || src[e] >= nnz) {  // only reachable with corrupt offsets
+                atomicOr(err, CWLB_DEVERR_OFFSETS);
+                src[e] = -1;
+            }
         }
-        new_col[p] = col[src];
-        new_val[p] = val[src];
+    }
+    int32_t cv[kGatherItems];
+    float vv[kGatherItems];
+#pragma unroll
+    for (int e = 0; e < kGatherItems; ++e) {
+        if (src[e] >= 0) {
+            cv[e] = __ldcs(col + src[e]);
+            vv[e] = __ldcs(val + src[e]);
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < kGatherItems; ++e) {
+        if (src[e] >= 0) {
+            const int32_t p = static_cast<int32_t>(c0) + e * kGatherThreads + threadIdx.x;
+            new_col[p] = cv[e];
+            new_val[p] = vv[e];
+        }
     }
 }
 
@@ -172,8 +214,14 @@ void launch_sort_by_degree(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int
     if (n_rows <= 0) return;
     cudaStream_t s = ctx->stream;
     const int64_t n = n_rows;
-    const int64_t n_tiles = ceil_div(n, kSortTile);
+    // About two tiles per SM per pass, 256..4096 items per tile.
+    const int rounds = static_cast<int>(std::min<int64_t>(
+        kSortMaxRounds,
+        std::max<int64_t>(1, ceil_div(n, int64_t{kSortThreads} * 2 *
+                                             ctx->props.multiProcessorCount))));
+    const int64_t n_tiles = ceil_div(n, int64_t{kSortThreads} * rounds);
     const int64_t hist_n = n_tiles * kRadix;
+    const int64_t n_chunks = ceil_div(nnz, kGatherChunk);
     // Scratch layout (256-byte aligned pieces).
     auto al = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
     const size_t b_keys = al(sizeof(uint32_t) * (n + 1));
@@ -181,13 +229,17 @@ void launch_sort_by_degree(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int
     const size_t b_hist = al(sizeof(int32_t) * hist_n);
     const size_t b_scan = al(std::max(scan_scratch_bytes<int32_t>(hist_n),
                                       scan_scratch_bytes<int32_t>(n + 1)));
-    char* p = static_cast<char*>(ctx->sort_scratch.ensure(2 * b_keys + b_vals + b_hist + b_scan + 256));
+    const size_t b_chunk = al(sizeof(int32_t) * std::max<int64_t>(n_chunks, 1));
+    char* p = static_cast<char*>(
+        ctx->sort_scratch.ensure(2 * b_keys + b_vals + b_hist + b_scan + 256 + 2 * b_chunk));
     uint32_t* keys_a = reinterpret_cast<uint32_t*>(p);
     uint32_t* keys_b = reinterpret_cast<uint32_t*>(p + b_keys);
     int32_t* vals_b = reinterpret_cast<int32_t*>(p + 2 * b_keys);
     int32_t* hist = reinterpret_cast<int32_t*>(p + 2 * b_keys + b_vals);
     void* scan_tmp = p + 2 * b_keys + b_vals + b_hist;
     unsigned int* d_max = reinterpret_cast<unsigned int*>(p + 2 * b_keys + b_vals + b_hist + b_scan);
+    int32_t* first_row = reinterpret_cast<int32_t*>(p + 2 * b_keys + b_vals + b_hist + b_scan + 256);
+    int32_t* last_row = first_row + b_chunk / sizeof(int32_t);
     int32_t* vals_a = origin;  // ping-pong through the caller's output
 
     CWLB_CUDA(cudaMemsetAsync(d_max, 0, sizeof(unsigned int), s));
@@ -206,12 +258,12 @@ void launch_sort_by_degree(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int
     int32_t* vout = vals_b;
     for (int pass = 0; pass < passes; ++pass) {
         const int shift = 8 * pass;
-        radix_hist_kernel<<<static_cast<unsigned>(n_tiles), kSortThreads, 0, s>>>(kin, n_rows, shift,
-                                                                                n_tiles, hist);
+        radix_hist_kernel<<<static_cast<unsigned>(n_tiles), kSortThreads, 0, s>>>(
+            kin, n_rows, shift, rounds, n_tiles, hist);
         CWLB_LAUNCH_CHECK("radix_hist_kernel");
         device_exclusive_scan<int32_t>(hist, hist, hist_n, scan_tmp, s);
         radix_scatter_kernel<<<static_cast<unsigned>(n_tiles), kSortThreads, 0, s>>>(
-            kin, vin, n_rows, shift, n_tiles, hist, kout, vout);
+            kin, vin, n_rows, shift, rounds, n_tiles, hist, kout, vout);
         CWLB_LAUNCH_CHECK("radix_scatter_kernel");
         std::swap(kin, kout);
         std::swap(vin, vout);
@@ -224,9 +276,13 @@ void launch_sort_by_degree(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int
     device_exclusive_scan<int32_t>(reinterpret_cast<const int32_t*>(kin), new_rowoff, n + 1,
                                    scan_tmp, s);
     if (nnz > 0) {
-        gather_rows_kernel<<<static_cast<unsigned>(ceil_div(nnz, kGatherChunk)), kGatherThreads, 0,
-                             s>>>(rowoff, col, val, origin, new_rowoff, n_rows, nnz, new_col,
-                                  new_val, ctx->d_error_flags);
+        CWLB_CUDA(cudaMemsetAsync(first_row, 0xff, 2 * b_chunk, s));  // -1: no row yet
+        chunk_rows_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, s>>>(
+            new_rowoff, n_rows, nnz, first_row, last_row, ctx->d_error_flags);
+        CWLB_LAUNCH_CHECK("chunk_rows_kernel");
+        gather_rows_kernel<<<static_cast<unsigned>(n_chunks), kGatherThreads, 0, s>>>(
+            rowoff, col, val, origin, new_rowoff, first_row, last_row, n_rows, nnz, new_col,
+            new_val, ctx->d_error_flags);
         CWLB_LAUNCH_CHECK("gather_rows_kernel");
     }
 }

@@ -140,10 +140,38 @@ def test_partition_unsorted_rows_vs_oracle(ctx, oracle):
 
 
 @pytest.mark.parametrize("n,maxdeg,hub", [(1, 5, 1), (7, 0, 1), (300, 40, 3), (5000, 20, 70000),
-                                          (20000, 300, 50), (70000, 3, 1)])
+                                          (20000, 300, 50), (70000, 3, 1), (300000, 12, 400),
+                                          (1 << 21, 2, 1)])
 def test_sort_vs_oracle(ctx, oracle, n, maxdeg, hub):
     rng = np.random.default_rng(n + maxdeg)
     rowoff, col, val = random_csr(rng, n, maxdeg, hubs=1, hub_factor=hub)
+    got = ctx.sortCSRByDegree(cs.CSR(rowoff, col, val))
+    want = oracle.sort_by_degree(rowoff, col, val)
+    assert np.array_equal(got.Origin_local, want[0])
+    assert np.array_equal(got.RowOffset, want[1])
+    assert np.array_equal(got.ColInd, want[2])
+    assert np.array_equal(got.Value, want[3])
+
+
+@pytest.mark.parametrize("case", ["exact_chunks", "ragged", "hub_only", "row_per_chunk"])
+def test_sort_chunk_boundaries(ctx, oracle, case):
+    """The row gather cuts the output into 2048-nonzero chunks: rows that end
+    or start exactly on a chunk boundary, empty rows between them, a single
+    row spanning many chunks and an nnz that is a multiple of the chunk."""
+    C = 2048
+    rng = np.random.default_rng(len(case))
+    if case == "exact_chunks":
+        deg = np.array([0, C, 0, 0, C // 2, C // 2, 3 * C, 0, C - 1, 1], np.int64)
+    elif case == "ragged":
+        deg = np.array([5, 0, C + 7, 0, 2 * C - 3, 11, 0, 1], np.int64)
+    elif case == "hub_only":
+        deg = np.array([0, 0, 40 * C + 123, 0], np.int64)
+    else:
+        deg = np.full(64, C, np.int64)
+        deg[::3] = 0
+    rowoff = np.concatenate([[0], np.cumsum(deg)]).astype(np.int32)
+    col = rng.integers(0, len(deg), int(rowoff[-1]), dtype=np.int32)
+    val = rng.random(int(rowoff[-1]), dtype=np.float32)
     got = ctx.sortCSRByDegree(cs.CSR(rowoff, col, val))
     want = oracle.sort_by_degree(rowoff, col, val)
     assert np.array_equal(got.Origin_local, want[0])
