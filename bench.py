@@ -470,6 +470,16 @@ def run_ours(args):
     bytes_local = compulsory_bytes(wl["n"], wl["nnz"], n_tasks, K, wl["distinct_cols"])
     peak, peak_kind = hbm_peak()
     achieved = bytes_local / per_launch / 1e9
+    # On-chip ceiling of the gather, measured on this GPU by the library's
+    # microbenchmark: uniformly random rows of K floats from a 48 MiB buffer,
+    # served from L2, with the aggregation's lane shapes and loads in flight.
+    ceiling = None
+    r4 = K // 4
+    if rank == 0 and K % 4 == 0 and 0 < r4 <= 256 and (r4 & (r4 - 1)) == 0:
+        l2_c = ctx.measure_gather_gbs(48, K, 20)
+        rate = 4 * wl["nnz"] * K / per_launch / 1e9
+        ceiling = {"l2_tb_s": round(l2_c / 1e3, 2), "frac_of_l2": round(rate / l2_c, 4),
+                   "what": "uniformly random rows of K floats from a 48 MiB (L2-resident) buffer"}
 
     e2e = None
     if not args.no_e2e:
@@ -554,6 +564,7 @@ def run_ours(args):
                          # mostly served by L2) and FP32 FMAs (nnz K).
                          "gather_bytes_per_launch": 4 * wl["nnz"] * K,
                          "gather_tb_s": round(4 * wl["nnz"] * K / per_launch / 1e12, 2),
+                         "gather_ceiling": ceiling,
                          "fma_per_launch": wl["nnz"] * K},
             "e2e": e2e,
             "gpu_launches": launches_per_step(flags, n_tasks) * args.steps,

@@ -75,6 +75,55 @@ __global__ void cal_atomic_kernel(float* __restrict__ counters, int64_t total_th
     }
 }
 
+// Gather ceiling: the aggregation's own access pattern without the sparse
+// bookkeeping.  Every group of L lanes reads whole rows of L*P float4s (the
+// rows of X at K = 4*L*P features) chosen uniformly at random among 2^row_bits
+// rows, with U rows (U*P = 8 float4s per lane) in flight, through the same
+// read-only path (__ldg) as the aggregation.  Row numbers are the top bits of
+// a per-group linear congruential sequence (x = 1664525 x + 1013904223 mod
+// 2^32, the Numerical Recipes constants) seeded by the lowbias32 hash
+// (C. Wellons, public domain) of the group id: three instructions a row and
+// no index array, so neither instruction issue nor index traffic limits the
+// rate.  A buffer that fits in L2 gives the rate for rows served from L2; one
+// far larger than L2 the rate for rows served from HBM.
+__device__ __forceinline__ uint32_t lowbias32(uint32_t x) {
+    x ^= x >> 16;
+    x *= 0x7feb352du;
+    x ^= x >> 15;
+    x *= 0x846ca68bu;
+    x ^= x >> 16;
+    return x;
+}
+
+template <int P, int U>
+__global__ void __launch_bounds__(256)
+    cal_gather_kernel(const float4* __restrict__ buf, int row_bits, int L, int iters,
+                      float* __restrict__ sink) {
+    const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
+    const int sub = static_cast<int>(tid % static_cast<uint32_t>(L));
+    const int64_t row4 = static_cast<int64_t>(L) * P;
+    const int shift = 32 - row_bits;  // row_bits in [1, 31]
+    uint32_t x = lowbias32(tid / static_cast<uint32_t>(L));
+    float s = 0.f;
+    for (int it = 0; it < iters; ++it) {
+        float4 v[U][P];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            x = x * 1664525u + 1013904223u;
+            const float4* q = buf + static_cast<int64_t>(x >> shift) * row4 + sub;
+#pragma unroll
+            for (int j = 0; j < P; ++j) v[u][j] = __ldg(q + j * L);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int j = 0; j < P; ++j) s += (v[u][j].x + v[u][j].y) + (v[u][j].z + v[u][j].w);
+    }
+    // The buffer holds zeros: the store never happens, but the compiler
+    // cannot prove it, so the loads stay.
+    if (s != 0.f) sink[tid % 1024] = s;
+}
+
 template <typename Launch>
 double mean_ms(cwlb_ctx* ctx, int repeat, Launch launch) {
     for (int w = 0; w < kCalWarmup; ++w) launch();
@@ -197,6 +246,52 @@ void measure_costs(cwlb_ctx* ctx, int K, int repeat, int WI, int data_MB, int wr
         out->C_atomic_ns = (avg_ms * 1e6) / ops * 10.0;
         out->atomic_writers_per_addr = groups_per_row;
     }
+}
+
+double measure_gather_gbs(cwlb_ctx* ctx, int buffer_MB, int row_floats, int repeat) {
+    cudaStream_t s = ctx->stream;
+    const int row4 = row_floats / 4;
+    // The aggregation's lane shapes: two float4s per lane where the row has
+    // at least two (16 lanes x 2 at K = 128, 4 x 2 at K = 32, 32 x 4 at K = 512).
+    const int L = std::max(1, std::min(row4 / 2, 32));  // lanes per row
+    const int P = row4 / L;                              // float4s per lane per row
+    const int64_t row_bytes = int64_t{row4} * 16;
+    // A power-of-two number of rows, 2 .. 2^31, at most the buffer's.
+    const int64_t fit = static_cast<int64_t>(buffer_MB) * 1024 * 1024 / row_bytes;
+    if (fit < 2) fail(CWLB_ERR_INVALID_ARGUMENT, "buffer_MB holds fewer than two rows.");
+    int row_bits = 1;
+    while (row_bits < 31 && (int64_t{1} << (row_bits + 1)) <= fit) ++row_bits;
+    const int64_t rows = int64_t{1} << row_bits;
+    DevMem buf(static_cast<size_t>(rows * row_bytes));
+    DevMem sink(sizeof(float) * 1024);
+    CWLB_CUDA(cudaMemsetAsync(buf.p, 0, static_cast<size_t>(rows * row_bytes), s));
+    // Rows in flight per lane group as in the aggregation: U*P = 8 float4s.
+    const int U = 8 / P;
+    const void* fn = P == 1   ? reinterpret_cast<const void*>(&cal_gather_kernel<1, 8>)
+                     : P == 2 ? reinterpret_cast<const void*>(&cal_gather_kernel<2, 4>)
+                     : P == 4 ? reinterpret_cast<const void*>(&cal_gather_kernel<4, 2>)
+                              : reinterpret_cast<const void*>(&cal_gather_kernel<8, 1>);
+    int per_sm = 0;
+    CWLB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, 0));
+    const unsigned blocks =
+        static_cast<unsigned>(ctx->props.multiProcessorCount) * static_cast<unsigned>(std::max(1, per_sm));
+    const int64_t groups = int64_t{blocks} * 256 / L;
+    // About 4 GB gathered per launch (at least one iteration).
+    const int iters = static_cast<int>(std::max<int64_t>(
+        1, (int64_t{1} << 32) / (groups * U * row_bytes)));
+    auto launch = [&] {
+        const float4* b = buf.as<float4>();
+        float* k = sink.as<float>();
+        switch (P) {
+            case 1: cal_gather_kernel<1, 8><<<blocks, 256, 0, s>>>(b, row_bits, L, iters, k); break;
+            case 2: cal_gather_kernel<2, 4><<<blocks, 256, 0, s>>>(b, row_bits, L, iters, k); break;
+            case 4: cal_gather_kernel<4, 2><<<blocks, 256, 0, s>>>(b, row_bits, L, iters, k); break;
+            default: cal_gather_kernel<8, 1><<<blocks, 256, 0, s>>>(b, row_bits, L, iters, k); break;
+        }
+    };
+    const double ms = mean_ms(ctx, repeat, launch);
+    const double bytes = static_cast<double>(groups) * iters * U * static_cast<double>(row_bytes);
+    return bytes / (ms * 1e-3) / 1e9;
 }
 
 }  // namespace cwlb

@@ -578,6 +578,23 @@ int cwlb_measure_spmm_costs(cwlb_ctx* ctx, int32_t K, int32_t repeat, int32_t WI
     });
 }
 
+int cwlb_measure_gather_gbs(cwlb_ctx* ctx, int32_t buffer_MB, int32_t row_floats,
+                            int32_t repeat, double* gbs) {
+    return guarded([&] {
+        check_ctx(ctx);
+        require(gbs != nullptr, CWLB_ERR_INVALID_ARGUMENT, "null output");
+        if (buffer_MB <= 0 || repeat <= 0) {
+            cwlb::fail(CWLB_ERR_INVALID_ARGUMENT, "All microbenchmark parameters must be positive.");
+        }
+        const int32_t row4 = row_floats / 4;
+        if (row_floats <= 0 || row_floats % 4 != 0 || row4 > 256 || (row4 & (row4 - 1)) != 0) {
+            cwlb::fail(CWLB_ERR_INVALID_ARGUMENT,
+                       "row_floats must be 4 times a power of two, at most 1024.");
+        }
+        *gbs = cwlb::measure_gather_gbs(ctx, buffer_MB, row_floats, repeat);
+    });
+}
+
 // ---------------------------------------------------------------------------
 // Host-side helpers (scalar arithmetic the reference also does on the host).
 

@@ -111,6 +111,8 @@ int64_t run_partition(cwlb_ctx* ctx, int32_t n_rows, const int32_t* d_rowoff,
 // The four calibration microbenchmarks (calibrate.cu).
 void measure_costs(cwlb_ctx* ctx, int K, int repeat, int WI, int data_MB, int writers,
                    cwlb_costs* out);
+// Random-row gather rate over a buffer_MB MiB device buffer, GB/s (calibrate.cu).
+double measure_gather_gbs(cwlb_ctx* ctx, int buffer_MB, int row_floats, int repeat);
 // Sets the calling thread's cwlb_last_error() message (defined in capi.cu).
 void set_last_error(const std::string& msg);
 

@@ -107,6 +107,7 @@ _sig("cwlb_wave_based_s", [_i64, _i32, _i32, C.POINTER(_i32)])
 _sig("cwlb_recommended_candidate_w", [C.c_uint64, C.POINTER(_i32)], None)
 _sig("cwlb_save_costs", [C.POINTER(cwlb_costs), C.c_char_p, _i32, _i32])
 _sig("cwlb_measure_spmm_costs", [_vp, _i32, _i32, _i32, _i32, _i32, C.POINTER(cwlb_costs)])
+_sig("cwlb_measure_gather_gbs", [_vp, _i32, _i32, _i32, C.POINTER(C.c_double)])
 _sig("cwlb_read_costs", [C.POINTER(cwlb_costs), C.c_char_p])
 _sig("cwlb_spmm_mean_reference_device", [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _vp])
 _sig("cwlb_validate_result", [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _i64,
@@ -321,6 +322,14 @@ class Context:
                                             atomic_target_writers, C.byref(c)))
         return SpmmCostParams(c.C_compute_ns, c.C_load_ns, c.C_store_ns, c.C_atomic_ns, c.K,
                               c.WI, c.repeat, c.atomic_writers_per_addr)
+
+    def measure_gather_gbs(self, buffer_MB=48, row_floats=128, repeat=20) -> float:
+        """Rate in GB/s of gathering uniformly random rows of row_floats floats
+        from a buffer_MB MiB device buffer: the ceiling for rows served from L2
+        when the buffer fits in L2, from HBM when it is far larger."""
+        g = _dbl()
+        _check(_lib.cwlb_measure_gather_gbs(self._h, buffer_MB, row_floats, repeat, C.byref(g)))
+        return g.value
 
     # ---- device-pointer entry points (asynchronous on the context stream) --
 

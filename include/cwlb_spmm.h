@@ -248,6 +248,22 @@ int cwlb_measure_spmm_costs(cwlb_ctx* ctx, int32_t K, int32_t repeat, int32_t WI
                             int32_t data_MB_for_load, int32_t atomic_target_writers,
                             cwlb_costs* out);
 
+/* Gather-rate microbenchmark (no reference counterpart; it supplies the
+ * ceiling for the aggregation's roofline).  Groups of lanes read whole rows of
+ * row_floats floats (the rows of X at K = row_floats), chosen uniformly at
+ * random among the largest power-of-two number of rows that fits in buffer_MB
+ * MiB of device memory, through the read-only data path, with eight 16-byte
+ * loads in flight per thread as in the aggregation; as many CTAs of 256
+ * threads as fit on every SM, about 4 GB per launch, 20 untimed and `repeat`
+ * timed launches.  *gbs
+ * receives bytes gathered / mean launch time in GB/s.  A buffer that fits in
+ * the 126 MB L2 (e.g. 48 MiB) gives the rate for rows served from L2; one far
+ * larger gives the rate for rows served from HBM.
+ * CWLB_ERR_INVALID_ARGUMENT unless buffer_MB and repeat are positive, the
+ * buffer holds two rows and row_floats is 4 times a power of two, at most 1024. */
+int cwlb_measure_gather_gbs(cwlb_ctx* ctx, int32_t buffer_MB, int32_t row_floats,
+                            int32_t repeat, double* gbs);
+
 /* ------------------------------------------------------------- validation */
 
 /* Float64 reference of the mean aggregation over an UNSORTED CSR (the

@@ -256,3 +256,20 @@ class _DevTasks:
     def __init__(self, ptr, count):
         self.__cuda_array_interface__ = {"shape": (count * 4,), "typestr": "<i4",
                                          "data": (ptr, False), "version": 3}
+
+
+@pytest.mark.parametrize("row_floats", [32, 128, 512])
+def test_gather_rate_microbenchmark(ctx, row_floats):
+    """The ceilings the bench reports: random rows gathered from a buffer that
+    fits in L2 arrive faster than from one far larger than L2 (HBM), and both
+    rates are plausible for a B200."""
+    l2 = ctx.measure_gather_gbs(48, row_floats, 5)
+    hbm = ctx.measure_gather_gbs(4096, row_floats, 5)
+    assert 500.0 < hbm < 10000.0, hbm
+    assert l2 > 1.5 * hbm, (l2, hbm)
+
+
+@pytest.mark.parametrize("args", [(0, 128, 1), (48, 0, 1), (48, 12, 1), (48, 2048, 1), (48, 128, 0)])
+def test_gather_rate_microbenchmark_rejects_bad_arguments(ctx, args):
+    with pytest.raises(ValueError):
+        ctx.measure_gather_gbs(*args)
