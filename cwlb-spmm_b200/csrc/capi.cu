@@ -8,6 +8,7 @@
 #include <cstring>
 #include <filesystem>
 #include <fstream>
+#include <future>
 #include <iomanip>
 #include <limits>
 #include <string>
@@ -49,7 +50,7 @@ void check_ctx(cwlb_ctx* ctx) {
 template <typename T>
 T* stage_h2d(cwlb_ctx* ctx, cwlb::DeviceBuffer& buf, const T* host, size_t count) {
     T* d = buf.as<T>(count);
-    if (count) CWLB_CUDA(cudaMemcpyAsync(d, host, sizeof(T) * count, cudaMemcpyHostToDevice, ctx->stream));
+    cwlb::copy_to_device(ctx, d, host, sizeof(T) * count, ctx->stream);
     return d;
 }
 
@@ -150,11 +151,8 @@ bool plan_pipeline(const int32_t* row_offset, int32_t n_rows, int32_t nnz, const
 }
 
 template <typename T>
-void copy_h2d(T* dst, const T* src, int64_t count, cudaStream_t s) {
-    if (count > 0) {
-        CWLB_CUDA(cudaMemcpyAsync(dst, src, sizeof(T) * static_cast<size_t>(count),
-                                  cudaMemcpyHostToDevice, s));
-    }
+void copy_h2d(cwlb_ctx* ctx, T* dst, const T* src, int64_t count, cudaStream_t s) {
+    if (count > 0) cwlb::copy_to_device(ctx, dst, src, sizeof(T) * static_cast<size_t>(count), s);
 }
 
 // Host-buffer aggregation.  All copies go on the context's copy stream: the
@@ -180,21 +178,25 @@ void spmm_host_staged(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
     bool launched[C] = {};
     int n_chunks = 1;
     try {
+        // The values are checked on other host threads while this one queues
+        // (or, for pageable memory, stages) the copies.
+        std::future<bool> unit = std::async(std::launch::async, all_ones, value,
+                                            static_cast<size_t>(nnz));
         // Copies start after whatever the compute stream has queued.
         CWLB_CUDA(cudaEventRecord(ctx->ev_start, ks));
         CWLB_CUDA(cudaStreamWaitEvent(cs, ctx->ev_start, 0));
-        copy_h2d(d_ro, row_offset, static_cast<int64_t>(n_rows) + 1, cs);
-        copy_h2d(d_org, origin, n_rows, cs);
-        copy_h2d(d_tasks, tasks, n_tasks, cs);
-        copy_h2d(d_H, H, h_rows * K, cs);
+        copy_h2d(ctx, d_ro, row_offset, static_cast<int64_t>(n_rows) + 1, cs);
+        copy_h2d(ctx, d_org, origin, n_rows, cs);
+        copy_h2d(ctx, d_tasks, tasks, n_tasks, cs);
+        copy_h2d(ctx, d_H, H, h_rows * K, cs);
         int64_t task_cut[C + 1] = {0, n_tasks}, nnz_cut[C + 1] = {0, nnz};
         if (plan_pipeline(row_offset, n_rows, nnz, tasks, n_tasks, task_cut, nnz_cut)) n_chunks = C;
         for (int c = 0; c < n_chunks; ++c) {
-            copy_h2d(d_col + nnz_cut[c], col_ind + nnz_cut[c], nnz_cut[c + 1] - nnz_cut[c], cs);
+            copy_h2d(ctx, d_col + nnz_cut[c], col_ind + nnz_cut[c], nnz_cut[c + 1] - nnz_cut[c], cs);
             CWLB_CUDA(cudaEventRecord(ctx->pipe_ready[c], cs));
         }
         const float* d_val = nullptr;
-        if (all_ones(value, static_cast<size_t>(nnz))) {
+        if (unit.get()) {
             if (ctx->ones_count < static_cast<size_t>(nnz)) {
                 float* d = ctx->ones.as<float>(static_cast<size_t>(nnz));
                 cwlb::launch_fill_ones(ctx, d, static_cast<size_t>(nnz));
@@ -204,7 +206,7 @@ void spmm_host_staged(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
         } else {
             float* dv = ctx->in_val.as<float>(static_cast<size_t>(nnz));
             for (int c = 0; c < n_chunks; ++c) {
-                copy_h2d(dv + nnz_cut[c], value + nnz_cut[c], nnz_cut[c + 1] - nnz_cut[c], cs);
+                copy_h2d(ctx, dv + nnz_cut[c], value + nnz_cut[c], nnz_cut[c + 1] - nnz_cut[c], cs);
                 CWLB_CUDA(cudaEventRecord(ctx->pipe_ready[c], cs));  // now after the values
             }
             d_val = dv;
@@ -220,10 +222,7 @@ void spmm_host_staged(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
             CWLB_CUDA(cudaEventRecord(ctx->pipe_t1[c], ks));
             launched[c] = true;
         }
-        if (out_count) {
-            CWLB_CUDA(cudaMemcpyAsync(out, d_out, sizeof(float) * out_count,
-                                      cudaMemcpyDeviceToHost, ks));
-        }
+        cwlb::copy_to_host(ctx, out, d_out, sizeof(float) * out_count, ks);
     } catch (...) {
         // No copy may still read the caller's arrays once the call returns.
         cudaStreamSynchronize(cs);
@@ -352,6 +351,7 @@ int cwlb_ctx_destroy(cwlb_ctx* ctx) {
     return guarded([&] {
         cudaSetDevice(ctx->device);
         if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+        cwlb::destroy_stager(ctx);
         for (cwlb::DeviceBuffer* b : {&ctx->in_rowoff, &ctx->in_col, &ctx->in_val, &ctx->in_origin,
                                       &ctx->in_H, &ctx->in_tasks, &ctx->out_buf, &ctx->sort_scratch,
                                       &ctx->part_scratch, &ctx->part_desc, &ctx->part_tasks,
@@ -501,13 +501,10 @@ int cwlb_sort_by_degree(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_
         float* d_nval = reinterpret_cast<float*>(d_ncol + nnz);
         cwlb::launch_sort_by_degree(ctx, n_rows, nnz, d_ro, d_col, d_val, d_org, d_nro, d_ncol, d_nval);
         cudaStream_t s = ctx->stream;
-        CWLB_CUDA(cudaMemcpyAsync(origin_local, d_org, 4 * n, cudaMemcpyDeviceToHost, s));
-        CWLB_CUDA(cudaMemcpyAsync(sorted_row_offset, d_nro, 4 * (n + 1), cudaMemcpyDeviceToHost, s));
-        if (nnz) {
-            CWLB_CUDA(cudaMemcpyAsync(sorted_col_ind, d_ncol, 4 * static_cast<size_t>(nnz), cudaMemcpyDeviceToHost, s));
-            CWLB_CUDA(cudaMemcpyAsync(sorted_value, d_nval, 4 * static_cast<size_t>(nnz), cudaMemcpyDeviceToHost, s));
-        }
-        CWLB_CUDA(cudaStreamSynchronize(s));
+        cwlb::copy_to_host(ctx, origin_local, d_org, 4 * n, s);
+        cwlb::copy_to_host(ctx, sorted_row_offset, d_nro, 4 * (n + 1), s);
+        cwlb::copy_to_host(ctx, sorted_col_ind, d_ncol, 4 * static_cast<size_t>(nnz), s);
+        cwlb::copy_to_host(ctx, sorted_value, d_nval, 4 * static_cast<size_t>(nnz), s);
         require(sorted_row_offset[n_rows] == nnz, CWLB_ERR_RUNTIME,
                 "DPL CPU degree reordering produced an inconsistent NNZ count.");
     });
@@ -543,10 +540,7 @@ int cwlb_partition(cwlb_ctx* ctx, int32_t n_rows, const int32_t* row_offset,
         if (max_tasks < cnt) {
             cwlb::fail(CWLB_ERR_BUFFER_TOO_SMALL, "task buffer too small");
         }
-        if (cnt) {
-            CWLB_CUDA(cudaMemcpyAsync(tasks, ctx->part_tasks.ptr, sizeof(cwlb_task) * cnt,
-                                      cudaMemcpyDeviceToHost, ctx->stream));
-        }
+        cwlb::copy_to_host(ctx, tasks, ctx->part_tasks.ptr, sizeof(cwlb_task) * cnt, ctx->stream);
         CWLB_CUDA(cudaStreamSynchronize(ctx->stream));
     });
 }

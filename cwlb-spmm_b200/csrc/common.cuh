@@ -56,6 +56,8 @@ struct DeviceBuffer {
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+struct HostStager;  // pinned bounce slots and copy threads (staging.cu)
+
 }  // namespace cwlb
 
 // The context (opaque in the C API).
@@ -81,6 +83,8 @@ struct cwlb_ctx {
     size_t ones_count = 0;
     // Fragment partials and their plan (CWLB_DETERMINISTIC).
     cwlb::DeviceBuffer det_scratch;
+    // Created by the first large copy of pageable caller memory.
+    cwlb::HostStager* stager = nullptr;
 };
 
 namespace cwlb {
@@ -93,6 +97,13 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
                       const int32_t* col, const float* val, const int32_t* origin,
                       const float* H, int64_t h_rows, int64_t K, const cwlb_task* tasks,
                       int64_t n_tasks, float* out, uint32_t flags);
+// Copies of caller memory for the host-buffer entry points (staging.cu).
+// copy_to_device is asynchronous on `s`; once it returns, the source may be
+// reused; copy_to_host returns when `dst` holds the data.  Large pageable
+// copies go through the context's pinned slots.
+void copy_to_device(cwlb_ctx* ctx, void* dst, const void* src, size_t bytes, cudaStream_t s);
+void copy_to_host(cwlb_ctx* ctx, void* dst, const void* src, size_t bytes, cudaStream_t s);
+void destroy_stager(cwlb_ctx* ctx);
 // Writes `count` floats of 1.0f (spmm.cu).
 void launch_fill_ones(cwlb_ctx* ctx, float* dst, size_t count);
 // Float64 reference of the aggregation over an unsorted CSR (spmm.cu).

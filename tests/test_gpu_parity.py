@@ -423,3 +423,48 @@ def test_chunked_host_call_matches_single_shot(ctx, oracle, unit, K):
     whole = [origin[r] for rs, re_, fo, ln in tk for r in range(rs, re_)
              if (fo if r == rs else 0) == 0 and (ln if (r == re_ - 1 and ln > 0) else deg[r]) == deg[r]]
     assert np.array_equal(chunked[whole], single[whole])
+
+
+def _pinned_copy(a):
+    torch = pytest.importorskip("torch")
+    t = torch.empty(a.shape, dtype=getattr(torch, str(a.dtype)), pin_memory=True)
+    out = t.numpy()
+    out[...] = a
+    return out, t
+
+
+def test_pageable_and_pinned_host_buffers_agree(ctx, oracle):
+    """Large host-buffer calls copy ordinary (pageable) memory through the
+    context's ring of four 32 MiB pinned slots, filled and drained by host
+    threads, and pinned memory directly.  With 160 MB column arrays (the ring
+    wraps) both give the oracle's degree sort bit for bit, and the aggregation
+    agrees between them on whole rows bit for bit and elsewhere to rounding."""
+    rng = np.random.default_rng(2024)
+    n = 400000
+    rowoff, col, val = random_csr(rng, n, 200, hubs=2, hub_factor=20)
+    assert col.nbytes > 4 * (32 << 20)
+    want = oracle.sort_by_degree(rowoff, col, val)
+    pinned = [_pinned_copy(a) for a in (rowoff, col, val)]
+    for ro_, col_, val_ in ((rowoff, col, val), tuple(p[0] for p in pinned)):
+        got = ctx.sortCSRByDegree(cs.CSR(ro_, col_, val_))
+        assert np.array_equal(got.Origin_local, want[0])
+        assert np.array_equal(got.RowOffset, want[1])
+        assert np.array_equal(got.ColInd, want[2])
+        assert np.array_equal(got.Value, want[3])
+    origin, srow, scol, sval = want
+    K = 16
+    H = rng.standard_normal((n, K)).astype(np.float32)
+    costs = cs.SpmmCostParams.from_list([0.1, 0.6, 0.4, 0.9])
+    order = cs.CSR_Order(srow, scol, sval, origin)
+    tasks = ctx.costWeightedTaskPartitioning(order, costs, cs.capacity_from_s(512, costs))
+    pageable_out, _ = ctx.spmmKernel(order, H, K, K, tasks)  # fresh (untouched) result pages
+    held = [_pinned_copy(a) for a in (srow, scol, sval, origin, H, np.zeros((n, K), np.float32))]
+    p_order = cs.CSR_Order(*(h[0] for h in held[:4]))
+    p_out = held[5][0]
+    ctx.spmmKernel(p_order, held[4][0], K, K, tasks, out=p_out)
+    deg = np.diff(srow)
+    whole = [origin[r] for rs, re_, fo, ln in tasks for r in range(rs, re_)
+             if (fo if r == rs else 0) == 0 and (ln if (r == re_ - 1 and ln > 0) else deg[r]) == deg[r]]
+    assert len(whole) > n // 2
+    assert np.array_equal(pageable_out[whole], p_out[whole])
+    np.testing.assert_allclose(pageable_out, p_out, rtol=1e-5, atol=1e-6)
