@@ -11,6 +11,7 @@
 #include <future>
 #include <iomanip>
 #include <limits>
+#include <sstream>
 #include <string>
 #include <thread>
 #include <vector>
@@ -690,6 +691,105 @@ int cwlb_read_costs(cwlb_costs* costs, const char* path) {
     costs->C_store_ns = v[2];
     costs->C_atomic_ns = v[3];
     return CWLB_OK;
+}
+
+int cwlb_save_costs_per_k(const cwlb_costs* costs, int64_t n, const char* path) {
+    namespace fs = std::filesystem;
+    if (!path || !*path || n < 0 || (n > 0 && !costs)) {
+        g_last_error = "invalid per-K cost table arguments";
+        return CWLB_ERR_RUNTIME;
+    }
+    for (int64_t i = 0; i < n; ++i) {
+        if (costs[i].K <= 0) {
+            g_last_error = "per-K cost entries need a positive K";
+            return CWLB_ERR_RUNTIME;
+        }
+    }
+    std::error_code ec;
+    const fs::path p(path);
+    if (p.has_parent_path() && !fs::exists(p.parent_path(), ec) &&
+        !fs::create_directories(p.parent_path(), ec) && ec) {
+        g_last_error = "cannot create the cost-file directory";
+        return CWLB_ERR_RUNTIME;
+    }
+    std::ofstream ofs(p, std::ios::out | std::ios::trunc);
+    if (!ofs.is_open()) {
+        g_last_error = "cannot open the per-K cost file";
+        return CWLB_ERR_RUNTIME;
+    }
+    ofs << "# K C_compute_ns C_load_ns C_store_ns C_atomic_ns\n" << std::fixed
+        << std::setprecision(6);
+    for (int64_t i = 0; i < n; ++i) {
+        ofs << costs[i].K << ' ' << costs[i].C_compute_ns << ' ' << costs[i].C_load_ns << ' '
+            << costs[i].C_store_ns << ' ' << costs[i].C_atomic_ns << "\n";
+    }
+    if (!ofs.good()) {
+        g_last_error = "per-K cost-file write failed";
+        return CWLB_ERR_RUNTIME;
+    }
+    return CWLB_OK;
+}
+
+int cwlb_read_costs_per_k(cwlb_costs* costs, int64_t max_entries, const char* path, int64_t* n) {
+    if (!path || !n || max_entries < 0 || (max_entries > 0 && !costs)) {
+        g_last_error = "null argument";
+        return CWLB_ERR_INVALID_ARGUMENT;
+    }
+    *n = 0;
+    std::ifstream ifs(path);
+    if (!ifs.is_open()) {
+        g_last_error = std::string("cannot read per-K cost file: ") + path;
+        return CWLB_ERR_RUNTIME;
+    }
+    std::string line;
+    int64_t count = 0, lineno = 0;
+    while (std::getline(ifs, line)) {
+        ++lineno;
+        const size_t b = line.find_first_not_of(" \t\r");
+        if (b == std::string::npos || line[b] == '#') continue;
+        std::istringstream ls(line);
+        long long k = 0;
+        double v[4];
+        std::string rest;
+        if (!(ls >> k >> v[0] >> v[1] >> v[2] >> v[3]) || (ls >> rest) || k <= 0 ||
+            k > INT32_MAX) {
+            g_last_error = std::string("malformed per-K cost file line ") +
+                           std::to_string(lineno) + ": " + path;
+            return CWLB_ERR_RUNTIME;
+        }
+        if (count < max_entries) {
+            cwlb_costs c{};
+            c.K = static_cast<int32_t>(k);
+            c.C_compute_ns = v[0];
+            c.C_load_ns = v[1];
+            c.C_store_ns = v[2];
+            c.C_atomic_ns = v[3];
+            costs[count] = c;
+        }
+        ++count;
+    }
+    *n = count;
+    if (count > max_entries && max_entries > 0) {
+        g_last_error = "per-K cost table larger than the buffer";
+        return CWLB_ERR_BUFFER_TOO_SMALL;
+    }
+    return CWLB_OK;
+}
+
+int64_t cwlb_costs_for_k(const cwlb_costs* costs, int64_t n, int64_t K) {
+    if (!costs || n <= 0 || K <= 0) return -1;
+    int64_t best = -1;
+    double best_d = 0.0;
+    for (int64_t i = 0; i < n; ++i) {
+        if (costs[i].K <= 0) continue;
+        const double d = std::fabs(std::log2(static_cast<double>(costs[i].K)) -
+                                   std::log2(static_cast<double>(K)));
+        if (best < 0 || d < best_d || (d == best_d && costs[i].K > costs[best].K)) {
+            best = i;
+            best_d = d;
+        }
+    }
+    return best;
 }
 
 }  // extern "C"

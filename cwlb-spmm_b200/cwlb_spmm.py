@@ -109,6 +109,9 @@ _sig("cwlb_save_costs", [C.POINTER(cwlb_costs), C.c_char_p, _i32, _i32])
 _sig("cwlb_measure_spmm_costs", [_vp, _i32, _i32, _i32, _i32, _i32, C.POINTER(cwlb_costs)])
 _sig("cwlb_measure_gather_gbs", [_vp, _i32, _i32, _i32, C.POINTER(C.c_double)])
 _sig("cwlb_read_costs", [C.POINTER(cwlb_costs), C.c_char_p])
+_sig("cwlb_save_costs_per_k", [C.POINTER(cwlb_costs), _i64, C.c_char_p])
+_sig("cwlb_read_costs_per_k", [C.POINTER(cwlb_costs), _i64, C.c_char_p, C.POINTER(_i64)])
+_sig("cwlb_costs_for_k", [C.POINTER(cwlb_costs), _i64, _i64], _i64)
 _sig("cwlb_spmm_mean_reference_device", [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _vp])
 _sig("cwlb_validate_result", [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _i64,
                               _i64, C.c_float, C.POINTER(_i32)])
@@ -455,3 +458,32 @@ def read_costs_one_per_line(filepath: str):
     if _lib.cwlb_read_costs(C.byref(c), filepath.encode()) != OK:
         return None
     return SpmmCostParams(c.C_compute_ns, c.C_load_ns, c.C_store_ns, c.C_atomic_ns)
+
+
+def save_costs_per_k(table, filepath: str) -> bool:
+    """Per-K cost table (costWrite --per-k): one line per entry, K then the
+    four costs; every entry needs a positive K."""
+    arr = (cwlb_costs * max(len(table), 1))(*[t.c() for t in table])
+    return _lib.cwlb_save_costs_per_k(arr, len(table), filepath.encode()) == OK
+
+
+def read_costs_per_k(filepath: str):
+    """The per-K table as a list of SpmmCostParams (K set), or None."""
+    n = _i64()
+    if _lib.cwlb_read_costs_per_k(None, 0, filepath.encode(), C.byref(n)) != OK:
+        return None
+    arr = (cwlb_costs * max(n.value, 1))()
+    if n.value and _lib.cwlb_read_costs_per_k(arr, n.value, filepath.encode(), C.byref(n)) != OK:
+        return None
+    return [SpmmCostParams(a.C_compute_ns, a.C_load_ns, a.C_store_ns, a.C_atomic_ns, a.K)
+            for a in arr[:n.value]]
+
+
+def costs_for_k(table, K: int) -> SpmmCostParams:
+    """The entry calibrated at the row width nearest to K on a log scale
+    (ties go to the larger width)."""
+    arr = (cwlb_costs * max(len(table), 1))(*[t.c() for t in table])
+    i = _lib.cwlb_costs_for_k(arr, len(table), int(K))
+    if i < 0:
+        raise ValueError("no per-K cost entry for this K")
+    return table[i]

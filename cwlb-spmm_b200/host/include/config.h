@@ -4,7 +4,7 @@
 //
 // The paths keep the reference's defaults (relative to a build/ working
 // directory); the dataset loader honours CWLB_DATASET_DIR, and the cwlb-spmm
-// tool CWLB_COSTFILE and CWLB_RESULTS.
+// and costWrite tools CWLB_COSTFILE, CWLB_COSTFILE_PER_K and CWLB_RESULTS.
 #include <cstddef>
 #include <stdexcept>
 #include <string>
@@ -17,6 +17,8 @@ using namespace std;
 inline const int WARMUPCOUNT = 20;
 inline const int LOOPCOUNT = 70;
 inline const std::string COSTFILEPATH = "../resources/spmm_costs.txt";
+// Per-K cost table (costWrite --per-k; an extension of the cost file).
+inline const std::string COSTFILEPATH_PER_K = "../resources/spmm_costs_per_k.txt";
 constexpr const char* DATA_CSR_FILE_PATH = "../resources/datasets/";
 
 namespace Defined {

@@ -71,6 +71,16 @@ bool save_costs_one_per_line(SpmmCostParams costs, const std::string& filepath =
                              bool append = false, int precision = 6);
 bool read_costs_one_per_line(SpmmCostParams& out, const std::string& filepath = COSTFILEPATH);
 
+// Per-K cost table, an extension of the cost file (cwlb_save_costs_per_k):
+// one "K C_compute C_load C_store C_atomic" line per calibrated row width K.
+bool save_costs_per_k(const std::vector<SpmmCostParams>& table,
+                      const std::string& filepath = COSTFILEPATH_PER_K);
+bool read_costs_per_k(std::vector<SpmmCostParams>& out,
+                      const std::string& filepath = COSTFILEPATH_PER_K);
+// The entry calibrated at the row width nearest to K on a log scale (ties go
+// to the larger width); std::invalid_argument for an empty table or K <= 0.
+SpmmCostParams costs_for_k(const std::vector<SpmmCostParams>& table, int K);
+
 std::vector<std::pair<int, float>> get_csr_row_elements(const CSR& csr, int row);
 
 // Compares a result against a caller-supplied reference with an absolute

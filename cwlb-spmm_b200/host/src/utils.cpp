@@ -126,6 +126,41 @@ bool read_costs_one_per_line(SpmmCostParams& out, const std::string& filepath) {
     return true;
 }
 
+bool save_costs_per_k(const std::vector<SpmmCostParams>& table, const std::string& filepath) {
+    std::vector<cwlb_costs> c;
+    c.reserve(table.size());
+    for (const SpmmCostParams& t : table) c.push_back(to_c(t));
+    return cwlb_save_costs_per_k(c.data(), static_cast<int64_t>(c.size()), filepath.c_str()) ==
+           CWLB_OK;
+}
+
+bool read_costs_per_k(std::vector<SpmmCostParams>& out, const std::string& filepath) {
+    int64_t n = 0;
+    if (cwlb_read_costs_per_k(nullptr, 0, filepath.c_str(), &n) != CWLB_OK) return false;
+    std::vector<cwlb_costs> c(static_cast<size_t>(n));
+    if (n > 0 && cwlb_read_costs_per_k(c.data(), n, filepath.c_str(), &n) != CWLB_OK) return false;
+    out.clear();
+    for (const cwlb_costs& e : c) {
+        SpmmCostParams p;
+        p.C_compute_ns = e.C_compute_ns;
+        p.C_load_ns = e.C_load_ns;
+        p.C_store_ns = e.C_store_ns;
+        p.C_atomic_ns = e.C_atomic_ns;
+        p.K = e.K;
+        out.push_back(p);
+    }
+    return true;
+}
+
+SpmmCostParams costs_for_k(const std::vector<SpmmCostParams>& table, int K) {
+    std::vector<cwlb_costs> c;
+    c.reserve(table.size());
+    for (const SpmmCostParams& t : table) c.push_back(to_c(t));
+    const int64_t i = cwlb_costs_for_k(c.data(), static_cast<int64_t>(c.size()), K);
+    if (i < 0) throw std::invalid_argument("no per-K cost entry for this K");
+    return table[static_cast<size_t>(i)];
+}
+
 std::vector<std::pair<int, float>> get_csr_row_elements(const CSR& csr, int row) {
     std::vector<std::pair<int, float>> e;
     const int rows = static_cast<int>(csr.RowOffset.size()) - 1;

@@ -12,11 +12,12 @@
 //
 // Extensions: CWLB_CSR_CACHE=1 loads the dataset through the binary cache
 // beside the text file (data.h), CWLB_DETERMINISTIC=1 merges split rows in a
-// fixed order (bit-reproducible outputs), and a trailing --verify checks every run's output with
-// validate_custom_csr_result (absolute tolerance 1e-4) against a float64
-// aggregation of the UNSORTED CSR computed on the device
-// (cwlb_spmm_mean_reference_device), and exits with status 1 on a mismatch.
-// Without it, output and exit status are the reference's.
+// fixed order (bit-reproducible outputs), CWLB_COSTS_PER_K=1 takes the costs
+// from the per-K table (costWrite --per-k) entry nearest to K, and a trailing
+// --verify checks every run's output with validate_custom_csr_result (absolute
+// tolerance 1e-4) against a float64 aggregation of the UNSORTED CSR computed on
+// the device (cwlb_spmm_mean_reference_device), and exits with status 1 on a
+// mismatch.  Without them, output and exit status are the reference's.
 //
 // Each S run partitions on the GPU, uploads the reordered CSR, X and the tasks
 // once, and times LOOPCOUNT aggregation launches with CUDA events (the first
@@ -361,7 +362,18 @@ int cli(int argc, char** argv) {
                                                                    : loadDatasetToCSR(ds, V, E);
     cwlb::Queue q;
     SpmmCostParams costs;
-    if (!read_costs_one_per_line(costs, cost_path())) {
+    const char* per_k = std::getenv("CWLB_COSTS_PER_K");
+    if (per_k && std::string(per_k) == "1") {
+        // Extension: the costs calibrated at the row width nearest to K.
+        const std::string path = env_or("CWLB_COSTFILE_PER_K", COSTFILEPATH_PER_K);
+        std::vector<SpmmCostParams> table;
+        if (!read_costs_per_k(table, path) || table.empty()) {
+            throw std::runtime_error("Cannot read per-K cost file: " + path +
+                                     ". Run ./costWrite --per-k first.");
+        }
+        costs = costs_for_k(table, K);
+        std::cerr << "costs: per-K table entry K=" << costs.K << " (" << path << ")\n";
+    } else if (!read_costs_one_per_line(costs, cost_path())) {
         throw std::runtime_error("Cannot read microbenchmark cost file: " + cost_path() +
                                  ". Run ./costWrite first.");
     }

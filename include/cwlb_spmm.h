@@ -306,6 +306,22 @@ int cwlb_save_costs(const cwlb_costs* costs, const char* path, int32_t append,
 /* read_costs_one_per_line (src/utils.cpp:1077-1092). */
 int cwlb_read_costs(cwlb_costs* costs, const char* path);
 
+/* Per-K cost table: an extension of the cost file (the reference calibrates at
+ * one K, 128 by default) with one line "K C_compute C_load C_store C_atomic"
+ * per calibrated row width, costs in fixed notation with 6 digits; lines that
+ * start with '#' are comments.  cwlb_save_costs_per_k writes the n entries in
+ * the given order (their K fields must be positive), creating the parent
+ * directory.  cwlb_read_costs_per_k sets *n to the number of entries in the
+ * file and copies up to max_entries of them into `costs` (NULL with
+ * max_entries 0 only counts); only K and the four costs are filled.  Both
+ * return CWLB_ERR_RUNTIME on I/O or format errors; reading returns
+ * CWLB_ERR_BUFFER_TOO_SMALL when the file holds more than max_entries. */
+int cwlb_save_costs_per_k(const cwlb_costs* costs, int64_t n, const char* path);
+int cwlb_read_costs_per_k(cwlb_costs* costs, int64_t max_entries, const char* path, int64_t* n);
+/* Index of the entry whose K is nearest to K on a log2 scale (ties go to the
+ * larger K); -1 for an empty table or K <= 0. */
+int64_t cwlb_costs_for_k(const cwlb_costs* costs, int64_t n, int64_t K);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,6 +13,7 @@ import sys
 import numpy as np
 import pytest
 
+import cwlb_spmm as cs
 import graphs
 from conftest import ROOT
 
@@ -37,7 +38,8 @@ os._exit(rc)
 
 def _env():
     env = dict(os.environ)
-    for k in ("CWLB_COSTFILE", "CWLB_DATASET_DIR", "CWLB_RESULTS"):
+    for k in ("CWLB_COSTFILE", "CWLB_DATASET_DIR", "CWLB_RESULTS", "CWLB_COSTS_PER_K",
+              "CWLB_COSTFILE_PER_K"):
         env.pop(k, None)
     return env
 
@@ -180,6 +182,28 @@ def test_cli_deterministic_mode_verifies(workdir):
                        capture_output=True, text=True, env=env, timeout=900)
     assert p.returncode == 0, p.stderr
     assert "Validation passed" in p.stdout
+
+
+def test_costwrite_per_k_table_and_cli_choice(workdir):
+    """costWrite --per-k calibrates once per listed K and writes the per-K
+    table; cwlb-spmm with CWLB_COSTS_PER_K=1 runs with the entry nearest to K
+    and leaves its stdout grammar unchanged."""
+    rc, out, err = run([COSTWRITE, "--per-k", "32,128", "5", "8192", "16", "4"], workdir / "build")
+    assert rc == 0, err
+    assert out.splitlines()[-1] == "Saved per-K cost parameters to: ../resources/spmm_costs_per_k.txt"
+    table = cs.read_costs_per_k(str(workdir / "resources" / "spmm_costs_per_k.txt"))
+    assert [t.K for t in table] == [32, 128]
+    assert all(v > 0 for t in table for v in (t.C_compute_ns, t.C_load_ns, t.C_store_ns,
+                                               t.C_atomic_ns))
+    env = _env()
+    env["CWLB_COSTS_PER_K"] = "1"
+    p = subprocess.run([CWLB, "g", "100", "--S", "8"], cwd=workdir / "build", capture_output=True,
+                       text=True, env=env, timeout=900)
+    assert p.returncode == 0, p.stderr
+    assert "costs: per-K table entry K=128" in p.stderr
+    assert re.search(r"SpMM time: [0-9.]+ us", p.stdout)
+    plain_rc, plain_out, _ = run([CWLB, "g", "100", "--S", "8"], workdir / "build")
+    assert plain_rc == 0 and template(plain_out)[:3] == template(p.stdout)[:3]
 
 
 def test_costwrite_writes_cost_file(workdir):
