@@ -592,7 +592,8 @@ def run_reference(args):
     oracle = Oracle()
     cfg = graphs.CONFIGS[args.config]
     dev = "cuda" if torch.cuda.is_available() else "cpu"
-    rowoff, col, val, X = graphs.build_config_torch(args.config, dev)  # input synthesis only
+    rowoff, col, val, X = graphs.build_config_torch(args.config, dev,  # input synthesis only
+                                                    scale_down=args.scale_down)
     rowoff, col, val, X = (t.cpu().numpy() for t in (rowoff, col, val, X))
     costs = np.loadtxt(COSTS_FILE)[:4]
     origin, srow, scol, sval = oracle.sort_by_degree(rowoff, col, val)
