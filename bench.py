@@ -3,8 +3,8 @@
 
 One step = one mean-aggregation pass out[i,:] = (1/deg_i) sum_j A_ij X[j,:]
 over the whole (sharded) graph of the configuration, with the reordered CSR,
-X and the task list resident in HBM.  The metric is BASELINE.json's:
-GFLOP/s (2 * nnz * K per step) with HBM GB/s against the measured roofline.
+X and the task list resident in HBM.  The metric: GFLOP/s (2 * nnz * K per
+step) with HBM GB/s against the measured roofline.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--S S]
   python bench.py --impl reference ...   (the CPU implementation of the path)
@@ -56,7 +56,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=2, help="BASELINE.json config (1-5)")
+    ap.add_argument("--config", type=int, default=2, help="benchmark configuration (1-5, graphs.CONFIGS)")
     ap.add_argument("--S", type=int, default=0, help="segment size; 0 = candidate search")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=12.0,

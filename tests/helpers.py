@@ -1,8 +1,8 @@
 """Shared helpers for the parity tests."""
 import numpy as np
 
-# Tolerance of the FP32 aggregation (max relative error
-# 1e-5 with FP32 accumulation).  Summation order differs from the reference
+# Tolerance of the FP32 aggregation: the path's target is a maximum relative
+# error of 1e-5 with FP32 accumulation.  Summation order differs from the reference
 # for split rows (atomic merge order) and for single-row tasks whose nonzeros
 # are spread over lane groups, so the bound is relative to the condition of
 # each output element: |gpu - ref64| <= REL_TOL * max(|ref64|, cond), where
