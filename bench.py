@@ -56,7 +56,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=2, help="benchmark configuration (1-5, graphs.CONFIGS)")
+    ap.add_argument("--config", type=int, default=2,
+                    help="benchmark configuration (1-5, graphs.CONFIGS)")
     ap.add_argument("--S", type=int, default=0, help="segment size; 0 = candidate search")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
