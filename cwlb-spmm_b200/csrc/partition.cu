@@ -874,7 +874,7 @@ int64_t partition_noalloc(cudaStream_t s, int32_t n_rows, const int32_t* d_rowof
     CWLB_CUDA(cudaMemcpyAsync(&w, wout, sizeof(w), cudaMemcpyDeviceToHost, s));
     CWLB_CUDA(cudaStreamSynchronize(s));
     if (w.fallback) return literal();
-    if (w.n_tasks > max_tasks || w.n_tasks <= 0) return w.n_tasks;
+    if (w.n_tasks > max_tasks || w.n_tasks <= 0 || !d_tasks) return w.n_tasks;
     expand_kernel<<<static_cast<unsigned>(ceil_div(w.n_tasks, 256)), 256, 0, s>>>(p, desc, w.n_desc,
                                                                                   w.n_tasks, d_tasks);
     CWLB_LAUNCH_CHECK("expand_kernel");
@@ -889,7 +889,10 @@ extern "C" int cwlb_partition_device_noalloc(void* cuda_stream, int32_t n_rows,
                                              double capacity, cwlb_task* d_tasks,
                                              int64_t max_tasks, int64_t* n_tasks) {
     try {
-        if (!costs || !n_tasks || (n_rows > 0 && !d_row_offset) || max_tasks < 0) {
+        // Checked before any launch: a NULL task buffer with a positive
+        // capacity would otherwise reach the expansion kernel's stores.
+        if (!costs || !n_tasks || (n_rows > 0 && !d_row_offset) || max_tasks < 0 ||
+            (max_tasks > 0 && !d_tasks)) {
             cwlb::fail(CWLB_ERR_INVALID_ARGUMENT, "cwlb_partition_device_noalloc: null argument");
         }
         *n_tasks = 0;
@@ -903,9 +906,6 @@ extern "C" int cwlb_partition_device_noalloc(void* cuda_stream, int32_t n_rows,
                        "cwlb_partition_device_noalloc: the task buffer holds " +
                            std::to_string(max_tasks) + " tasks, " + std::to_string(cnt) +
                            " are needed");
-        }
-        if (cnt > 0 && !d_tasks) {
-            cwlb::fail(CWLB_ERR_INVALID_ARGUMENT, "cwlb_partition_device_noalloc: null task buffer");
         }
         return CWLB_OK;
     } catch (const cwlb::Failure& e) {

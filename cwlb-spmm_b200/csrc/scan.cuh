@@ -57,11 +57,12 @@ __global__ void __launch_bounds__(kScanThreads)
     if (threadIdx.x == 0) tile_sums[blockIdx.x] = total;
 }
 
-// Each thread owns kScanItems consecutive items (blocked layout).
+// Each thread owns kScanItems consecutive items (blocked layout).  in and out
+// may be the same array (no __restrict__ on them): every thread reads all of
+// its items before it writes any, and no other thread touches them.
 template <typename T>
 __global__ void __launch_bounds__(kScanThreads)
-    scan_apply_kernel(const T* __restrict__ in, int64_t n, const T* __restrict__ tile_offsets,
-                      T* __restrict__ out) {
+    scan_apply_kernel(const T* in, int64_t n, const T* __restrict__ tile_offsets, T* out) {
     __shared__ T sw[kScanThreads / 32];
     const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanTile +
                          static_cast<int64_t>(threadIdx.x) * kScanItems;

@@ -130,3 +130,30 @@ def test_noalloc_rejects_sizes_beyond_its_limits():
     out = torch.empty((2, 4), dtype=torch.int32, device="cuda")
     rc, n = _call_noalloc(d_ro, 40, costs, cs.capacity_from_s(4, costs), out, 2)
     assert rc == cs.ERR_BUFFER_TOO_SMALL and n > 2
+
+
+def test_noalloc_rejects_a_null_task_buffer_before_any_launch():
+    # Host-side check only: a NULL buffer with a positive capacity is refused
+    # before the call looks up its scratch or launches a kernel.
+    ro = sorted_rowoff_from_degrees(np.arange(40))
+    d_ro = torch.from_numpy(ro).cuda()
+    costs = cs.SpmmCostParams(0.1, 0.2, 0.3, 0.4)
+    rc, n = _call_noalloc(d_ro, 40, costs, cs.capacity_from_s(4, costs), None, 5)
+    assert rc == cs.ERR_INVALID_ARGUMENT
+    assert "null argument" in cs._lib.cwlb_last_error().decode()
+    assert n == -1  # the count is not written on a rejected call
+
+
+def test_noalloc_rejects_more_distinct_degrees_than_its_run_limit():
+    # Degrees 0..16384 give 16385 runs of equal degree, one more than the
+    # scratch holds.  Only the offsets are read, so nnz (1.3e8) costs nothing.
+    max_runs = 16384  # CWLB_NOALLOC_MAX_RUNS in include/cwlb_spmm.h
+    ro = sorted_rowoff_from_degrees(np.arange(max_runs + 1))
+    d_ro = torch.from_numpy(ro).cuda()
+    costs = cs.SpmmCostParams(0.1, 0.2, 0.3, 0.4)
+    out = torch.full((64, 4), -7, dtype=torch.int32, device="cuda")
+    rc, _ = _call_noalloc(d_ro, len(ro) - 1, costs, cs.capacity_from_s(32, costs), out, 64)
+    torch.cuda.synchronize()
+    assert rc == cs.ERR_INVALID_ARGUMENT
+    assert "distinct row degrees" in cs._lib.cwlb_last_error().decode()
+    assert (out.cpu().numpy() == -7).all()  # the task buffer is untouched
