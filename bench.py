@@ -328,6 +328,95 @@ def compulsory_bytes(n, nnz, n_tasks, K, x_rows):
 
 
 # ---------------------------------------------------------------------------
+# output check of the timed configuration (after the timed region)
+
+PARITY_TOL = 1e-5  # condition-relative, as tests/helpers.py
+
+
+def _max_cond_rel(out, ref, cond):
+    """max |out - ref| / max(|ref|, cond) (inf where the scale is 0 and the
+    error is not); all float64 numpy arrays of the same shape."""
+    err = np.abs(out - ref)
+    scale = np.maximum(np.abs(ref), cond)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        rel = np.where(scale > 0, err / scale, np.where(err > 0, np.inf, 0.0))
+    return float(rel.max()) if rel.size else 0.0
+
+
+def parity_check(ctx, wl, out, sample_rows=4096, hub_rows=16, seed=0):
+    """Check the timed output, outside the timed region, two ways.
+
+    * every row: against the library's float64 device reference over the
+      UNSORTED CSR (cwlb_spmm_mean_reference_device, which shares no code with
+      the sort, the partitioner or the task kernels), with the condition
+      scale (1/deg) sum |a x| from the same kernel over |values| and |X|;
+    * sampled rows (the `hub_rows` largest rows, the hub tail, plus random
+      rows up to `sample_rows`): against the CPU oracle's float64 mean
+      (oracle/cwlb_oracle.cpp, the restatement of src/parallelMatrix.cpp:
+      151-236), run on a sub-CSR of those rows.
+    Both use the tolerance of the parity tests, |out - ref| <= 1e-5 * max(
+    |ref|, cond) per element."""
+    import torch
+    from oracle import Oracle
+    n, nnz, K = wl["n"], wl["nnz"], wl["K"]
+    X = wl["X"]
+    dev = X.device
+    res = {"tol": PARITY_TOL, "what": "max |out-ref| / max(|ref|, (1/deg) sum |a x|)"}
+    if n == 0:
+        res.update(rows_checked_device_f64=0, rows_checked_oracle=0, max_rel_device_f64=0.0,
+                   max_rel_oracle=0.0, passed=True)
+        return res
+    ro, col, val = wl["rowoff"], wl["col"], wl["val"]
+    ref = torch.empty((n, K), dtype=torch.float32, device=dev)
+    cond = torch.empty((n, K), dtype=torch.float32, device=dev)
+    ctx.spmm_mean_reference_device(n, nnz, ro.data_ptr(), col.data_ptr(), val.data_ptr(),
+                                   X.data_ptr(), X.shape[0], K, ref.data_ptr())
+    aval, ax = val.abs(), X.abs()
+    ctx.spmm_mean_reference_device(n, nnz, ro.data_ptr(), col.data_ptr(), aval.data_ptr(),
+                                   ax.data_ptr(), X.shape[0], K, cond.data_ptr())
+    torch.cuda.synchronize()
+    del aval, ax
+    worst = 0.0
+    for r0 in range(0, n, 1 << 16):  # float64 on the device, a block of rows at a time
+        r1 = min(n, r0 + (1 << 16))
+        o, rf, cd = (t[r0:r1].double() for t in (out, ref, cond))
+        sc = torch.maximum(rf.abs(), cd)
+        err = (o - rf).abs()
+        rel = torch.where(sc > 0, err / sc, torch.where(err > 0, torch.full_like(err, np.inf),
+                                                        torch.zeros_like(err)))
+        worst = max(worst, float(rel.max()))
+    del ref, cond
+    res.update(rows_checked_device_f64=n, max_rel_device_f64=worst)
+
+    # Sampled rows against the CPU oracle.
+    deg = (ro[1:] - ro[:-1]).long()
+    hubs = torch.topk(deg, min(hub_rows, n)).indices
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    rnd = torch.randperm(n, generator=g)[:max(0, sample_rows - hubs.numel())].to(dev)
+    rows = torch.unique(torch.cat([hubs, rnd]))
+    starts, d = ro[rows].long(), deg[rows]
+    sub_ro = torch.zeros(rows.numel() + 1, dtype=torch.int64, device=dev)
+    torch.cumsum(d, 0, out=sub_ro[1:])
+    total = int(sub_ro[-1])
+    idx = torch.repeat_interleave(starts - sub_ro[:-1], d) + torch.arange(total, device=dev)
+    sub_col, sub_val = col[idx], val[idx]
+    uniq, inv = torch.unique(sub_col, return_inverse=True)
+    x_sub = X[uniq.long()].cpu().numpy()
+    oracle = Oracle()
+    ident = np.arange(rows.numel(), dtype=np.int32)
+    ref64, cond64 = oracle.spmm_mean_f64(sub_ro.to(torch.int32).cpu().numpy(),
+                                         inv.to(torch.int32).cpu().numpy(),
+                                         sub_val.cpu().numpy(), ident, x_sub)
+    got = out[rows].double().cpu().numpy()
+    w_or = _max_cond_rel(got, ref64, cond64)
+    res.update(rows_checked_oracle=int(rows.numel()), nnz_checked_oracle=total,
+               hub_rows=int(hubs.numel()), max_rel_oracle=w_or,
+               passed=bool(worst <= PARITY_TOL and w_or <= PARITY_TOL))
+    return res
+
+
+# ---------------------------------------------------------------------------
 # CPU baseline: the oracle (restatement of the reference's kernel semantics)
 
 def cpu_baseline(wl, tasks_np, target_seconds):
@@ -462,6 +551,11 @@ def run_ours(args):
     assert ctx.take_device_errors() == 0
     if wl.get("x_sharded"):
         assert torch.equal(wl["X"], x_full), "all-gathered X differs from the source"
+    # The timed output, checked outside the timed region (every rank its shard).
+    parity = parity_check(ctx, wl, out)
+    parity_all = allgather_values(1.0 if parity["passed"] else 0.0, world)
+    parity["ranks_passed"] = int(sum(parity_all))
+    log(f"[rank {rank}] parity: {parity}")
     t_max = allreduce_max(t_local, world)
     per_rank_ms = [round(v / args.steps * 1e3, 4) for v in allgather_values(t_local, world)]
 
@@ -568,6 +662,7 @@ def run_ours(args):
                          "gather_ceiling": ceiling,
                          "fma_per_launch": wl["nnz"] * K},
             "e2e": e2e,
+            "parity": parity,
             "gpu_launches": launches_per_step(flags, n_tasks) * args.steps,
             "clocks": clocks,
         }
