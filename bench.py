@@ -9,12 +9,14 @@ step) with HBM GB/s against the measured roofline.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--S S]
   python bench.py --impl reference ...   (the CPU implementation of the path)
 
-Multi-GPU (torchrun, one rank per GPU): every rank builds the same graph,
+Multi-GPU (torchrun, one rank per GPU): every rank builds the same graph and
+hands it to the library's shard entry point (cwlb_shard_create_device), which
 takes a contiguous, cost-balanced block of ORIGINAL rows (X replicated), sorts
-and partitions it on its GPU, and aggregates it; no collective on the data
-path.  Total work is fixed as N grows ("strong" scaling).  With --x-sharded,
-X starts row-sharded (each rank holds the rows it owns, as a prior layer's
-output leaves it) and every timed step all-gathers it over NCCL first.
+and partitions it on the rank's GPU; each step aggregates the block
+(cwlb_shard_aggregate_device); no collective on the data path.  Total work
+is fixed as N grows ("strong" scaling).  With --x-sharded, X starts
+row-sharded (each rank holds the rows it owns, as a prior layer's output
+leaves it) and every timed step all-gathers it over NCCL first.
 
 Outside the timed region: graph synthesis (torch, seeded), degree sort,
 partition (both on the GPU), the S choice (the reference's --candidates
@@ -230,10 +232,15 @@ def build_workload(cfg_id, device, world, rank, costs, scale_down=1):
     ro = (rowoff[a:b + 1] - e0).contiguous()
     sub_col = col[e0:e1].contiguous()
     sub_val = val[e0:e1].contiguous()
-    return dict(rowoff=ro, col=sub_col, val=sub_val, X=X, n=b - a, nnz=e1 - e0, row0=a,
-                bounds=bounds,
-                nnz_total=int(rowoff[-1]), n_total=rowoff.numel() - 1, K=X.shape[1],
-                distinct_cols=int(torch.unique(sub_col).numel()) if e1 > e0 else 0)
+    wl = dict(rowoff=ro, col=sub_col, val=sub_val, X=X, n=b - a, nnz=e1 - e0, row0=a,
+              bounds=bounds,
+              nnz_total=int(rowoff[-1]), n_total=rowoff.numel() - 1, K=X.shape[1],
+              distinct_cols=int(torch.unique(sub_col).numel()) if e1 > e0 else 0)
+    if world > 1:
+        # The whole graph stays on every rank's GPU: the library's shard
+        # entry point (cwlb_shard_create_device) cuts and sorts its block.
+        wl["full"] = (rowoff, col, val)
+    return wl
 
 
 def device_prepare(ctx, wl):
@@ -298,9 +305,25 @@ def launches_per_step(flags, n_tasks):
     return n
 
 
+def make_shard(ctx, wl, costs, S, rank, world):
+    """N > 1: this rank's shard through the library's multi-GPU entry point
+    (cut by cwlb_shard_bounds, sorted, partitioned and checked on this GPU)."""
+    import cwlb_spmm as cs
+    ro, col, val = wl["full"]
+    sh = cs.Shard.from_device(ctx, wl["n_total"], wl["nnz_total"], ro.data_ptr(), col.data_ptr(),
+                              val.data_ptr(), costs, cs.capacity_from_s(S, costs), rank, world)
+    assert (sh.row_begin, sh.row_end) == tuple(wl["bounds"][rank]), "shard cut differs"
+    assert sh.nnz == wl["nnz"]
+    return sh
+
+
 def run_step(ctx, wl, tasks, n_tasks, out, flags):
     if wl.get("x_sharded"):
         shards.gather_rows(wl["X"], wl["bounds"])
+    if wl.get("shard") is not None:
+        wl["shard"].aggregate_device(wl["X"].data_ptr(), wl["X"].shape[0], wl["K"],
+                                     out.data_ptr(), flags & 2)  # DETERMINISTIC only
+        return
     ctx.spmm_mean_device(wl["n"], wl["nnz"], wl["sro"].data_ptr(), wl["scol"].data_ptr(),
                          wl["sval"].data_ptr(), wl["org"].data_ptr(), wl["X"].data_ptr(),
                          wl["X"].shape[0], wl["K"], tasks.data_ptr(), n_tasks, out.data_ptr(),
@@ -419,10 +442,13 @@ def parity_check(ctx, wl, out, sample_rows=4096, hub_rows=16, seed=0):
 # ---------------------------------------------------------------------------
 # CPU baseline: the oracle (restatement of the reference's kernel semantics)
 
-def cpu_baseline(wl, tasks_np, target_seconds):
-    """Time the oracle's OpenMP aggregation on this host: a contiguous slice of
-    the task list (the whole list when it is short), repeated until about
-    `target_seconds` of CPU work has been timed."""
+def cpu_baseline(wl, tasks_np, target_seconds, one_pass=False):
+    """Time the oracle's OpenMP aggregation on this host's cores over the
+    WHOLE task list, repeated until about `target_seconds` of CPU work has
+    been timed (at least one pass; exactly one with one_pass).  Only when one
+    pass would take more than twice the target is a contiguous slice of the
+    task list timed instead, and the line says which fraction of the
+    nonzeros it covered."""
     from oracle import Oracle
     oracle = Oracle()
     srow = wl["sro"].cpu().numpy()
@@ -434,6 +460,7 @@ def cpu_baseline(wl, tasks_np, target_seconds):
     threads = os.cpu_count() or 1
     task_nnz = _task_nnz(srow, tasks_np)
     n_t = len(tasks_np)
+    total_nnz = int(task_nnz.sum())
 
     def run(t0, t1):
         sub = np.ascontiguousarray(tasks_np[t0:t1])
@@ -441,27 +468,32 @@ def cpu_baseline(wl, tasks_np, target_seconds):
         oracle.spmm_mean(srow, scol, sval, org, X, sub, n_threads=threads)
         return time.perf_counter() - s, int(task_nnz[t0:t1].sum())
 
-    # probe ~1% of the tasks to size a slice of ~target/4 seconds
-    start = n_t // 3
-    probe = max(1, min(n_t - start, n_t // 100 + 1))
-    dt, nz = run(start, start + probe)
-    rate = max(nz, 1) / max(dt, 1e-6)
-    csum = np.cumsum(task_nnz)
-    want = rate * target_seconds / 4
-    t0 = start if csum[-1] - csum[start] > want else 0
-    base = csum[t0 - 1] if t0 > 0 else 0
-    t1 = min(n_t, int(np.searchsorted(csum, base + want)) + 1)
+    t0, t1 = 0, n_t
+    if not one_pass:
+        # probe ~1% of the tasks to estimate the time of a whole pass
+        start = n_t // 3
+        probe = max(1, min(n_t - start, n_t // 100 + 1))
+        dt, nz = run(start, start + probe)
+        rate = max(nz, 1) / max(dt, 1e-6)
+        if total_nnz / rate > 2 * target_seconds:
+            csum = np.cumsum(task_nnz)
+            want = rate * target_seconds / 2
+            t0 = start if csum[-1] - csum[start] > want else 0
+            base = csum[t0 - 1] if t0 > 0 else 0
+            t1 = min(n_t, int(np.searchsorted(csum, base + want)) + 1)
     tot_t, tot_nz, reps = 0.0, 0, 0
-    while tot_t < target_seconds and reps < 1000:
+    while reps == 0 or (not one_pass and tot_t < target_seconds and reps < 1000):
         dt, nz = run(t0, t1)
         tot_t += dt
         tot_nz += nz
         reps += 1
+    covered = tot_nz // reps
+    what = ("the whole task list" if (t0, t1) == (0, n_t) else
+            f"tasks [{t0}, {t1}) = {covered / max(total_nnz, 1):.1%} of the nonzeros")
     return {"value": 2.0 * tot_nz * K / tot_t / 1e9, "unit": "GFLOP/s", "cores": threads,
-            "kind": "port",
-            "sample": f"oracle spmm_mean over tasks [{t0}, {t1}) = {tot_nz // reps} of "
-                      f"{wl['nnz']} nnz (K={K}), repeated {reps}x, {tot_t:.1f} s, "
-                      f"{threads} OpenMP threads"}
+            "kind": "port", "fraction_of_nnz": round(covered / max(total_nnz, 1), 4),
+            "sample": f"oracle spmm_mean over {what} ({covered} of {total_nnz} nnz, K={K}, "
+                      f"{n_t} tasks), {reps} pass(es), {tot_t:.1f} s, {threads} OpenMP threads"}
 
 
 def _task_nnz(srow, tasks):
@@ -511,6 +543,10 @@ def run_ours(args):
         candidates = [cs.wave_based_s(wl["nnz_total"], cus, w) for w in ws]
     best = None
     for S in candidates:
+        if world > 1:
+            if wl.get("shard") is not None:
+                wl["shard"].close()
+            wl["shard"] = make_shard(ctx, wl, costs, S, rank, world)
         tasks, n_tasks, cap, chk = partition(ctx, wl, costs, S)
         flags = cs.ROWS_COVERED if (chk["uncovered_rows"] == 0 and chk["bad_tasks"] == 0 and
                                     chk["nnz_coverage_errors"] == 0) else 0
@@ -533,6 +569,12 @@ def run_ours(args):
     covered = chk["uncovered_rows"] == 0 and chk["bad_tasks"] == 0 and chk["nnz_coverage_errors"] == 0
     flags = cs.ROWS_COVERED if covered else 0
     flags |= cs.DETERMINISTIC if args.deterministic else 0
+    if world > 1:
+        if wl.get("shard") is not None:
+            wl["shard"].close()
+        wl["shard"] = make_shard(ctx, wl, costs, S, rank, world)
+        # The shard's task list is the partition of the same block.
+        assert wl["shard"].n_tasks == n_tasks, "shard task count differs"
 
     for _ in range(args.warmup):
         run_step(ctx, wl, tasks, n_tasks, out, flags)
@@ -557,6 +599,11 @@ def run_ours(args):
     parity["ranks_passed"] = int(sum(parity_all))
     log(f"[rank {rank}] parity: {parity}")
     t_max = allreduce_max(t_local, world)
+    if world > 1:
+        import torch.distributed as dist
+        pg_world = dist.get_world_size()
+    else:
+        pg_world = 1
     per_rank_ms = [round(v / args.steps * 1e3, 4) for v in allgather_values(t_local, world)]
 
     flops_total = 2.0 * wl["nnz_total"] * K
@@ -576,7 +623,7 @@ def run_ours(args):
         ceiling = {"l2_tb_s": round(l2_c / 1e3, 2), "frac_of_l2": round(rate / l2_c, 4),
                    "what": "uniformly random rows of K floats from a 48 MiB (L2-resident) buffer"}
 
-    e2e = None
+    e2e = e2e_weighted = None
     if not args.no_e2e:
         # e2e: host buffers through the reference-facing call (spmmKernel)
         sro = wl["sro"].cpu().pin_memory()
@@ -605,6 +652,25 @@ def run_ours(args):
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "values_copied": not unit_values,
                "ms_per_step": round(t_e2e / e2e_steps * 1e3, 3)}
+        # The same call on a weighted copy of the graph (values in [0.5, 1.5),
+        # not all one): the values cross PCIe every step as well.
+        g = torch.Generator(device="cpu")
+        g.manual_seed(5)
+        sval_w = (torch.rand(sval.shape, generator=g) + 0.5).pin_memory()
+        order_w = cs.CSR_Order(sro.numpy(), scol.numpy(), sval_w.numpy(), org.numpy())
+        call(order_w, Xh.numpy(), K, K, th.numpy(), out=outh.numpy())  # warm
+        barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            call(order_w, Xh.numpy(), K, K, th.numpy(), out=outh.numpy())
+        t_w = allreduce_max(time.perf_counter() - t0, world)
+        e2e_weighted = {"value": round(flops_total / (t_w / e2e_steps) / 1e9, 2),
+                        "unit": "GFLOP/s", "h2d_bytes_per_step": h2d + (sval.numel() * 4
+                                                                         if unit_values else 0),
+                        "d2h_bytes_per_step": d2h, "values_copied": True,
+                        "ms_per_step": round(t_w / e2e_steps * 1e3, 3),
+                        "values": "uniform [0.5, 1.5), seed 5"}
+        del order_w, sval_w
         # The whole per-graph pipeline a reference user runs (main.cpp:
         # load -> sortCSRByDegree -> costWeightedTaskPartitioning -> spmmKernel),
         # from an unsorted host CSR in ordinary (pageable) memory; the second
@@ -640,6 +706,7 @@ def run_ours(args):
                        "rows": wl["n_total"], "nnz": wl["nnz_total"], "K": K, "S": S,
                        "n_tasks_rank0": n_tasks, "costs": os.path.relpath(COSTS_FILE, ROOT),
                        "parallelism": f"row shards x{world}" if world > 1 else "single GPU",
+                       "process_group_world_size": pg_world,
                        "ms_per_step_by_rank": per_rank_ms,
                        "split_row_merge": "deterministic" if args.deterministic else "atomic",
                        "x": ("row-sharded; one NCCL all-gather per step, inside the timing"
@@ -662,6 +729,7 @@ def run_ours(args):
                          "gather_ceiling": ceiling,
                          "fma_per_launch": wl["nnz"] * K},
             "e2e": e2e,
+            "e2e_weighted": e2e_weighted,
             "parity": parity,
             "gpu_launches": launches_per_step(flags, n_tasks) * args.steps,
             "clocks": clocks,
@@ -669,6 +737,8 @@ def run_ours(args):
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
+    if wl.get("shard") is not None:
+        wl["shard"].close()
     ctx.close()
     if world > 1:
         import torch.distributed as dist
@@ -705,12 +775,13 @@ def run_reference(args):
     wl = dict(sro=torch.from_numpy(srow), scol=torch.from_numpy(scol),
               sval=torch.from_numpy(sval), org=torch.from_numpy(origin), X=torch.from_numpy(X),
               K=K, nnz=nnz, n=len(origin))
-    per_step = min(15.0, max(0.5, 120.0 / max(args.steps + args.warmup, 1)))
+    # One step = one pass over the whole task list (the reference's one
+    # spmmKernel call, main.cpp:372-391), timed on all host cores.
     for _ in range(args.warmup):
-        cpu_baseline(wl, tasks, min(per_step, 2.0))
+        cpu_baseline(wl, tasks, 0.0, one_pass=True)
     vals, samples = [], []
     for _ in range(args.steps):
-        r = cpu_baseline(wl, tasks, per_step)
+        r = cpu_baseline(wl, tasks, 0.0, one_pass=True)
         vals.append(r["value"])
         samples.append(r)
     v = statistics.mean(vals)

@@ -96,7 +96,8 @@ constexpr uint32_t kFlagOutCleared = 1u << 31;
 void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                       const int32_t* col, const float* val, const int32_t* origin,
                       const float* H, int64_t h_rows, int64_t K, const cwlb_task* tasks,
-                      int64_t n_tasks, float* out, uint32_t flags);
+                      int64_t n_tasks, float* out, uint32_t flags,
+                      const int32_t* sched = nullptr);
 // Copies of caller memory for the host-buffer entry points (staging.cu).
 // copy_to_device is asynchronous on `s`; once it returns, the source may be
 // reused; copy_to_host returns when `dst` holds the data.  Large pageable

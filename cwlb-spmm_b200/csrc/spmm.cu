@@ -66,6 +66,9 @@ struct SpmmArgs {
     // last) instead of atomics.  nullptr: atomic mode.
     float* __restrict__ frag;
     const int32_t* __restrict__ frag_pos;
+    // Optional launch order: warp slot i runs task sched[i] (a permutation of
+    // [0, n_tasks)); nullptr runs task i.
+    const int32_t* __restrict__ sched;
 };
 
 __device__ __forceinline__ void raise_err(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
@@ -338,8 +341,13 @@ template <int L, int V, bool kStage>
 __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
     constexpr int G = VecCfg<L, V>::G;
     const int lane = threadIdx.x & 31;
-    const int64_t t = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
-    if (t >= a.n_tasks) return;
+    const int64_t slot = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
+    if (slot >= a.n_tasks) return;
+    const int64_t t = a.sched ? static_cast<int64_t>(__ldg(a.sched + slot)) : slot;
+    if (t < 0 || t >= a.n_tasks) {  // an order entry outside the task list
+        if ((threadIdx.x & 31) == 0) raise_err(a.err, CWLB_DEVERR_ROW_RANGE);
+        return;
+    }
     cwlb_task tk;
     if (!load_task(a, t, tk)) return;
 
@@ -781,7 +789,7 @@ void pick_vec_shape(int64_t K4, int& L, int& V) {
 void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                       const int32_t* col, const float* val, const int32_t* origin,
                       const float* H, int64_t h_rows, int64_t K, const cwlb_task* tasks,
-                      int64_t n_tasks, float* out, uint32_t flags) {
+                      int64_t n_tasks, float* out, uint32_t flags, const int32_t* sched) {
     if (K <= 0 || n_rows <= 0) return;
     cudaStream_t s = ctx->stream;
     const bool covered = (flags & CWLB_ROWS_COVERED) != 0;
@@ -806,6 +814,7 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
     a.n_rows = n_rows;
     a.nnz = nnz;
     a.write_empty = covered ? 1 : 0;
+    a.sched = sched;
 
     if (covered) {
         dim3 grid(static_cast<unsigned>(ceil_div(n_tasks, kThreads)));

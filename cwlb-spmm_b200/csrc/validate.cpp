@@ -33,6 +33,18 @@ struct Mismatch {
     std::vector<float> dense_col;
 };
 
+// The report below (get_csr_row_elements and validate_custom_csr_result,
+// src/utils.cpp:1095-1265 of hhx-C/CWLB-SpMM) restates the reference's
+// checks, their order and its output text, which callers compare byte for
+// byte.  That code is Copyright (c) 2026, Hongxing He, Guanlin He and Chunlin
+// Li, under the BSD 3-Clause License: redistribution and use in source and
+// binary forms, with or without modification, are permitted provided that
+// the copyright notice, this list of conditions and the disclaimer are
+// retained; neither the names of the copyright holders nor of the
+// contributors may be used to endorse or promote derived products without
+// prior written permission.  THE SOFTWARE IS PROVIDED "AS IS", WITHOUT
+// WARRANTY OF ANY KIND.
+
 // get_csr_row_elements (src/utils.cpp:1095-1115): empty outside [0, rows).
 std::vector<std::pair<int32_t, float>> row_entries(const int32_t* row_offset, int64_t len,
                                                    const int32_t* col, const float* val,

@@ -113,6 +113,19 @@ _sig("cwlb_save_costs_per_k", [C.POINTER(cwlb_costs), _i64, C.c_char_p])
 _sig("cwlb_read_costs_per_k", [C.POINTER(cwlb_costs), _i64, C.c_char_p, C.POINTER(_i64)])
 _sig("cwlb_costs_for_k", [C.POINTER(cwlb_costs), _i64, _i64], _i64)
 _sig("cwlb_spmm_mean_reference_device", [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _vp])
+_sig("cwlb_shard_bounds", [_i32, _vp, C.POINTER(cwlb_costs), _i32, _vp])
+_sig("cwlb_shard_create", [_vp, _i32, _i32, _vp, _vp, _vp, C.POINTER(cwlb_costs), _dbl, _i32,
+                           _i32, C.POINTER(_vp)])
+_sig("cwlb_shard_create_device", [_vp, _i32, _i32, _vp, _vp, _vp, C.POINTER(cwlb_costs), _dbl,
+                                  _i32, _i32, C.POINTER(_vp)])
+_sig("cwlb_shard_info", [_vp, C.POINTER(_i32), C.POINTER(_i32), C.POINTER(_i32), C.POINTER(_i64),
+                         C.POINTER(_i32)])
+_sig("cwlb_shard_tasks", [_vp, C.POINTER(_vp)])
+_sig("cwlb_shard_aggregate_device", [_vp, _vp, _i64, _i64, _vp, _u32])
+_sig("cwlb_shard_destroy", [_vp])
+_sig("cwlb_spmm_mean_multi", [C.POINTER(_vp), _i32, _i32, _i32, _vp, _vp, _vp, _vp, _i64, _i64,
+                              C.POINTER(cwlb_costs), _dbl, _vp, C.POINTER(_dbl)])
+_sig("cwlb_gather_rows_multi", [C.POINTER(_vp), _i32, C.POINTER(_vp), _i64, _i64, _vp])
 _sig("cwlb_validate_result", [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _i64,
                               _i64, C.c_float, C.POINTER(_i32)])
 
@@ -366,6 +379,111 @@ class Context:
         _check(_lib.cwlb_tasks_check(self._h, n_rows, nnz, d_rowoff, d_tasks, n_tasks,
                                      C.byref(bad), C.byref(unc), C.byref(nz)))
         return dict(bad_tasks=bad.value, uncovered_rows=unc.value, nnz_coverage_errors=nz.value)
+
+
+# ---------------------------------------------------------------------------
+# several GPUs of one node (no counterpart in the reference, which runs on one
+# sycl::queue, main.cpp:514-516)
+
+def shard_bounds(row_offset, costs: SpmmCostParams, n_shards: int) -> np.ndarray:
+    """Cut points of the cost-balanced contiguous row shards (n_shards + 1
+    ints): shard s = original rows [b[s], b[s+1]), equal summed whole-row
+    weight (Cc + Cl) * deg + Cs (src/utils.cpp:850-852).  Host code."""
+    ro = np.ascontiguousarray(row_offset, np.int32)
+    n = max(len(ro) - 1, 0)
+    b = np.zeros(n_shards + 1, np.int32)
+    c = costs.c()
+    _check(_lib.cwlb_shard_bounds(n, _p(ro), C.byref(c), n_shards, _p(b)))
+    return b
+
+
+class Shard:
+    """One GPU's resident share of a multi-GPU aggregation: original rows
+    [row_begin, row_end) sorted by degree and partitioned on that GPU."""
+
+    def __init__(self, ctx: "Context", handle):
+        self.ctx = ctx
+        self._h = handle
+        rb, re_, nz, nt, seg = _i32(), _i32(), _i32(), _i64(), _i32()
+        _check(_lib.cwlb_shard_info(self._h, C.byref(rb), C.byref(re_), C.byref(nz), C.byref(nt),
+                                    C.byref(seg)))
+        self.row_begin, self.row_end, self.nnz = rb.value, re_.value, nz.value
+        self.n_tasks, self.segment_size = nt.value, seg.value
+
+    @classmethod
+    def from_host(cls, ctx: "Context", csr: CSR, costs: SpmmCostParams, capacity: float,
+                  shard: int, n_shards: int) -> "Shard":
+        h = _vp()
+        c = costs.c()
+        _check(_lib.cwlb_shard_create(ctx.handle, csr.rows, csr.nnz, _p(csr.RowOffset),
+                                      _p(csr.ColInd), _p(csr.Value), C.byref(c), float(capacity),
+                                      shard, n_shards, C.byref(h)))
+        return cls(ctx, h)
+
+    @classmethod
+    def from_device(cls, ctx: "Context", n_rows, nnz, d_rowoff, d_col, d_val,
+                    costs: SpmmCostParams, capacity: float, shard: int, n_shards: int) -> "Shard":
+        h = _vp()
+        c = costs.c()
+        _check(_lib.cwlb_shard_create_device(ctx.handle, n_rows, nnz, d_rowoff, d_col, d_val,
+                                             C.byref(c), float(capacity), shard, n_shards,
+                                             C.byref(h)))
+        return cls(ctx, h)
+
+    @property
+    def rows(self) -> int:
+        return self.row_end - self.row_begin
+
+    def tasks_ptr(self) -> int:
+        p = _vp()
+        _check(_lib.cwlb_shard_tasks(self._h, C.byref(p)))
+        return p.value or 0
+
+    def aggregate_device(self, d_H, h_rows, K, d_out, flags=0):
+        """Rows [row_begin, row_end) of the mean aggregation into d_out
+        ((rows, K), device memory); asynchronous on the context's stream."""
+        _check(_lib.cwlb_shard_aggregate_device(self._h, d_H, h_rows, K, d_out, flags))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.cwlb_shard_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def spmm_mean_multi(ctxs, csr: CSR, H, costs: SpmmCostParams, capacity: float, out=None):
+    """The whole pipeline (sort -> partition -> aggregation) over the GPUs of
+    `ctxs`, one host thread each, from an UNSORTED host CSR and host H to the
+    (rows, K) output in ORIGINAL row order.  Returns (out, time_us), time_us
+    the largest per-GPU device time of the aggregation."""
+    H = np.ascontiguousarray(H, np.float32)
+    K = H.shape[1] if H.ndim == 2 else 0
+    n = csr.rows
+    if out is None:
+        out = np.zeros((n, K), np.float32)
+    elif out.shape != (n, K) or out.dtype != np.float32 or not out.flags.c_contiguous:
+        raise ValueError("out must be a C-contiguous float32 (rows, K) array")
+    arr = (_vp * len(ctxs))(*[c.handle for c in ctxs])
+    tm = _dbl()
+    c = costs.c()
+    _check(_lib.cwlb_spmm_mean_multi(arr, len(ctxs), n, csr.nnz, _p(csr.RowOffset),
+                                     _p(csr.ColInd), _p(csr.Value), _p(H), H.shape[0], K,
+                                     C.byref(c), float(capacity), _p(out), C.byref(tm)))
+    return out, tm.value
+
+
+def gather_rows_multi(ctxs, d_ptrs, rows: int, K: int, bounds):
+    """All-gather of a row-sharded (rows, K) float32 matrix over the contexts'
+    GPUs by peer copies; d_ptrs[g] holds rows [bounds[g], bounds[g+1])."""
+    b = np.ascontiguousarray(bounds, np.int32)
+    arr = (_vp * len(ctxs))(*[c.handle for c in ctxs])
+    ptrs = (_vp * len(d_ptrs))(*d_ptrs)
+    _check(_lib.cwlb_gather_rows_multi(arr, len(ctxs), ptrs, rows, K, _p(b)))
 
 
 # ---------------------------------------------------------------------------

@@ -33,6 +33,7 @@
 #include <iomanip>
 #include <iostream>
 #include <limits>
+#include <memory>
 #include <random>
 #include <sstream>
 #include <stdexcept>
@@ -65,6 +66,16 @@ std::array<int, 3> candidate_waves(uint64_t nnz) {
     return {w[0], w[1], w[2]};
 }
 
+// positive_count, search_interval, grid_by_count, grid_by_step and
+// ask_yes_no restate main.cpp:98-184 of hhx-C/CWLB-SpMM (integer grid
+// formulas and a prompt loop whose output callers compare byte for byte).
+// That code is Copyright (c) 2026, Hongxing He, Guanlin He and Chunlin Li,
+// under the BSD 3-Clause License: redistribution and use in source and binary
+// forms, with or without modification, are permitted provided that the
+// copyright notice, this list of conditions and the disclaimer are retained;
+// neither the names of the copyright holders nor of the contributors may be
+// used to endorse or promote derived products without prior written
+// permission.  THE SOFTWARE IS PROVIDED "AS IS", WITHOUT WARRANTY OF ANY KIND.
 int positive_count(const std::string& text) {
     std::size_t used = 0;
     const int v = std::stoi(text, &used);
@@ -172,7 +183,22 @@ struct RunResult {
     std::vector<double> samples;
 };
 
-class Runner {
+// One partition + timing loop (run_single_s, main.cpp:338-412) at segment size s.
+class RunnerBase {
+public:
+    virtual ~RunnerBase() = default;
+    virtual RunResult run(int s, bool keep_samples) = 0;
+};
+
+void print_iteration(int it, const std::string& device, int K, double us) {
+    const bool warm = it < WARMUPCOUNT;
+    std::cout << std::fixed << std::setprecision(6) << (warm ? "[Warm-up " : "[Iteration ")
+              << (warm ? it + 1 : it - WARMUPCOUNT + 1) << '/'
+              << (warm ? WARMUPCOUNT : LOOPCOUNT - WARMUPCOUNT) << "] device=" << device
+              << " K=" << K << " time=" << us << " us\n";
+}
+
+class Runner : public RunnerBase {
 public:
     Runner(cwlb::Queue& q, const CSR_Order& g, const Defined::RowMajorMatrixXf& x, int K,
            const SpmmCostParams& costs, const CSR* verify_against = nullptr)
@@ -190,7 +216,7 @@ public:
         cudaEventDestroy(e1_);
     }
 
-    RunResult run(int s, bool keep_samples) {
+    RunResult run(int s, bool keep_samples) override {
         RunResult r;
         r.s = s;
         r.capacity = capacity_from_s(s, costs_);
@@ -226,12 +252,8 @@ public:
                 cudaEventElapsedTime(&ms, e0_, e1_);
                 us = ms * 1e3;
             }
-            const bool warm = it < WARMUPCOUNT;
-            std::cout << std::fixed << std::setprecision(6) << (warm ? "[Warm-up " : "[Iteration ")
-                      << (warm ? it + 1 : it - WARMUPCOUNT + 1) << '/'
-                      << (warm ? WARMUPCOUNT : LOOPCOUNT - WARMUPCOUNT) << "] device=" << q_.name()
-                      << " K=" << K_ << " time=" << us << " us\n";
-            if (!warm) {
+            print_iteration(it, q_.name(), K_, us);
+            if (it >= WARMUPCOUNT) {
                 sum += us;
                 if (keep_samples) r.samples.push_back(us);
             }
@@ -294,6 +316,174 @@ private:
     cudaEvent_t e0_{}, e1_{};
 };
 
+// CWLB_GPUS=N (N >= 2): the same loop over N GPUs of this node through the
+// library's shard entry points (cwlb_shard_create / cwlb_shard_aggregate_device):
+// GPU g sorts, partitions and aggregates the g-th cost-balanced block of
+// original rows with X replicated; an iteration's time is the largest of the
+// GPUs' event times (all GPUs launch before any is waited for).
+class MultiRunner : public RunnerBase {
+public:
+    MultiRunner(const std::vector<int>& devices, const CSR& graph,
+                const Defined::RowMajorMatrixXf& x, int K, const SpmmCostParams& costs,
+                bool verify)
+        : graph_(graph), x_host_(x), K_(K), verify_(verify), rows_(x.rows()) {
+        costs_ = cwlb_costs{costs.C_compute_ns, costs.C_load_ns, costs.C_store_ns,
+                            costs.C_atomic_ns, costs.K, costs.WI, costs.repeat,
+                            costs.atomic_writers_per_addr};
+        for (int dev : devices) gpus_.emplace_back(new Gpu(dev, x));
+        name_ = gpus_[0]->q.name() + " x" + std::to_string(devices.size());
+    }
+    ~MultiRunner() override {
+        for (auto& g : gpus_) drop_shard(*g);
+    }
+
+    RunResult run(int s, bool keep_samples) override {
+        RunResult r;
+        r.s = s;
+        r.capacity = cwlb_capacity_from_s(s, &costs_);
+        const int G = static_cast<int>(gpus_.size());
+        const int32_t n = static_cast<int32_t>(graph_.RowOffset.size()) - 1;
+        const int32_t nnz = static_cast<int32_t>(graph_.ColInd.size());
+        for (int g = 0; g < G; ++g) {
+            Gpu& d = *gpus_[g];
+            drop_shard(d);
+            cwlb::check(cwlb_shard_create(d.q.ctx(), n, nnz, graph_.RowOffset.data(),
+                                          graph_.ColInd.data(), graph_.Value.data(), &costs_,
+                                          r.capacity, g, G, &d.shard));
+            int64_t nt = 0;
+            cwlb::check(cwlb_shard_info(d.shard, &d.row_begin, &d.row_end, nullptr, &nt, nullptr));
+            r.tasks += static_cast<std::size_t>(nt);
+            d.out.reset(new DeviceArrayOn<float>(d.dev, static_cast<std::size_t>(d.row_end - d.row_begin) * K_));
+        }
+        const char* det = std::getenv("CWLB_DETERMINISTIC");
+        const uint32_t flags = (det && std::string(det) == "1") ? CWLB_DETERMINISTIC : 0u;
+        double sum = 0.0;
+        for (int it = 0; it < LOOPCOUNT; ++it) {
+            for (auto& dp : gpus_) {
+                Gpu& d = *dp;
+                cudaSetDevice(d.dev);
+                cudaEventRecord(d.e0, d.stream());
+                cwlb::check(cwlb_shard_aggregate_device(d.shard, d.x->p, rows_, K_, d.out->p, flags));
+                cudaEventRecord(d.e1, d.stream());
+            }
+            double us = 0.0;
+            for (auto& dp : gpus_) {
+                Gpu& d = *dp;
+                cudaSetDevice(d.dev);
+                cudaEventSynchronize(d.e1);
+                float ms = 0.0f;
+                cudaEventElapsedTime(&ms, d.e0, d.e1);
+                us = std::max(us, 1e3 * ms);
+            }
+            print_iteration(it, name_, K_, us);
+            if (it >= WARMUPCOUNT) {
+                sum += us;
+                if (keep_samples) r.samples.push_back(us);
+            }
+        }
+        for (auto& dp : gpus_) {
+            uint32_t dev_err = 0;
+            cwlb::check(cwlb_ctx_take_device_errors(dp->q.ctx(), &dev_err));
+            if (dev_err) throw std::invalid_argument("invalid CSR or task indices detected on the device");
+        }
+        r.mean_us = sum / static_cast<double>(LOOPCOUNT - WARMUPCOUNT);
+        if (verify_) verify(s);
+        return r;
+    }
+
+private:
+    template <typename T>
+    struct DeviceArrayOn {
+        int dev;
+        T* p = nullptr;
+        DeviceArrayOn(int device, std::size_t n, const T* src = nullptr) : dev(device) {
+            cudaSetDevice(dev);
+            if (cudaMalloc(&p, sizeof(T) * std::max<std::size_t>(n, 1)) != cudaSuccess) {
+                throw std::runtime_error("device allocation failed");
+            }
+            if (src && n && cudaMemcpy(p, src, sizeof(T) * n, cudaMemcpyHostToDevice) != cudaSuccess) {
+                throw std::runtime_error("host to device copy failed");
+            }
+        }
+        ~DeviceArrayOn() {
+            cudaSetDevice(dev);
+            if (p) cudaFree(p);
+        }
+    };
+    struct Gpu {
+        int dev;
+        cwlb::Queue q;
+        std::unique_ptr<DeviceArrayOn<float>> x, out;
+        cwlb_shard* shard = nullptr;
+        int32_t row_begin = 0, row_end = 0;
+        cudaEvent_t e0{}, e1{};
+        Gpu(int device, const Defined::RowMajorMatrixXf& xh) : dev(device), q(device) {
+            x.reset(new DeviceArrayOn<float>(device, static_cast<std::size_t>(xh.rows()) * xh.cols(),
+                                             xh.data()));
+            cudaSetDevice(dev);
+            cudaEventCreate(&e0);
+            cudaEventCreate(&e1);
+        }
+        ~Gpu() {
+            cudaSetDevice(dev);
+            cudaEventDestroy(e0);
+            cudaEventDestroy(e1);
+        }
+        cudaStream_t stream() const { return static_cast<cudaStream_t>(cwlb_ctx_stream(q.ctx())); }
+    };
+    static void drop_shard(Gpu& d) {
+        if (d.shard) cwlb_shard_destroy(d.shard);
+        d.shard = nullptr;
+    }
+
+    // The assembled output (each GPU's block of rows) against the float64
+    // device aggregation of the unsorted CSR on the first GPU.
+    void verify(int s) {
+        const std::size_t nk = static_cast<std::size_t>(rows_) * static_cast<std::size_t>(K_);
+        Defined::RowMajorMatrixXf result(rows_, K_);
+        for (auto& dp : gpus_) {
+            Gpu& d = *dp;
+            cudaSetDevice(d.dev);
+            const std::size_t b = static_cast<std::size_t>(d.row_end - d.row_begin) * K_;
+            if (b && cudaMemcpy(result.data() + static_cast<std::size_t>(d.row_begin) * K_, d.out->p,
+                                sizeof(float) * b, cudaMemcpyDeviceToHost) != cudaSuccess) {
+                throw std::runtime_error("device to host copy failed");
+            }
+        }
+        if (reference_.rows() != rows_ || reference_.cols() != K_) {
+            Gpu& d = *gpus_[0];
+            DeviceArrayOn<int> ro(d.dev, graph_.RowOffset.size(), graph_.RowOffset.data());
+            DeviceArrayOn<int> col(d.dev, graph_.ColInd.size(), graph_.ColInd.data());
+            DeviceArrayOn<float> val(d.dev, graph_.Value.size(), graph_.Value.data());
+            DeviceArrayOn<float> ref(d.dev, nk);
+            cwlb::check(cwlb_spmm_mean_reference_device(
+                d.q.ctx(), static_cast<int32_t>(graph_.RowOffset.size()) - 1,
+                static_cast<int32_t>(graph_.ColInd.size()), ro.p, col.p, val.p, d.x->p, rows_, K_,
+                ref.p));
+            d.q.wait();
+            reference_ = Defined::RowMajorMatrixXf(rows_, K_);
+            if (nk && cudaMemcpy(reference_.data(), ref.p, sizeof(float) * nk,
+                                 cudaMemcpyDeviceToHost) != cudaSuccess) {
+                throw std::runtime_error("device to host copy failed");
+            }
+        }
+        std::cout << "[Verify] S=" << s << ' ';
+        if (!validate_custom_csr_result(result, reference_, graph_, x_host_, 1e-4f)) {
+            throw std::runtime_error("Verification failed for S=" + std::to_string(s) + ".");
+        }
+    }
+
+    const CSR& graph_;
+    const Defined::RowMajorMatrixXf& x_host_;
+    int K_;
+    bool verify_;
+    long rows_;
+    cwlb_costs costs_{};
+    std::string name_;
+    std::vector<std::unique_ptr<Gpu>> gpus_;
+    Defined::RowMajorMatrixXf reference_;
+};
+
 void print_result(const std::string& ds, int V, int E, const SpmmCostParams& c, const RunResult& r) {
     std::cout << std::fixed << std::setprecision(6) << "Dataset: " << ds << '\n'
               << "V: " << V << ", E: " << E << '\n'
@@ -302,9 +492,61 @@ void print_result(const std::string& ds, int V, int E, const SpmmCostParams& c, 
               << " C_store_ns=" << c.C_store_ns << " C_atomic_ns=" << c.C_atomic_ns << '\n';
 }
 
+// Devices of the multi-GPU extension from CWLB_DEVICES (comma-separated
+// ordinals) or CWLB_GPUS (a count: ordinals 0..N-1); one device by default.
+std::vector<int> multi_gpu_devices() {
+    int avail = 0;
+    cudaGetDeviceCount(&avail);
+    std::vector<int> devs;
+    if (const char* list = std::getenv("CWLB_DEVICES")) {
+        std::stringstream ss(list);
+        std::string item;
+        while (std::getline(ss, item, ',')) {
+            int d = -1;
+            try {
+                d = std::stoi(item);
+            } catch (const std::exception&) {
+                d = -1;
+            }
+            if (d < 0 || d >= avail) {
+                throw std::invalid_argument("CWLB_DEVICES must list device ordinals below " +
+                                            std::to_string(avail) + ".");
+            }
+            devs.push_back(d);
+        }
+    } else if (const char* g = std::getenv("CWLB_GPUS")) {
+        const int n = std::atoi(g);
+        if (n < 1 || n > avail) {
+            throw std::invalid_argument("CWLB_GPUS must be between 1 and the number of GPUs (" +
+                                        std::to_string(avail) + ").");
+        }
+        for (int d = 0; d < n; ++d) devs.push_back(d);
+    }
+    if (devs.empty()) devs.push_back(0);
+    return devs;
+}
+
 enum class Mode { Wave, FixedS, Sweep, Candidates, Search };
 
+// Extension: `cwlb-spmm --dump-features ROWS COLS FILE` writes the X this
+// CLI would use for a graph of ROWS vertices at K = COLS (features() above,
+// float32, row-major, raw bytes) and exits; no device is touched.  Tests use
+// it to compare the CLI's X bit for bit with the reference's.
+int dump_features(int argc, char** argv) {
+    if (argc != 5) throw std::invalid_argument("Usage: ./cwlb-spmm --dump-features ROWS COLS FILE");
+    const int rows = std::stoi(argv[2]), cols = std::stoi(argv[3]);
+    if (rows < 0 || cols < 0) throw std::invalid_argument("ROWS and COLS must not be negative.");
+    const Defined::RowMajorMatrixXf x = features(rows, cols);
+    std::ofstream f(argv[4], std::ios::binary | std::ios::trunc);
+    if (!f) throw std::runtime_error(std::string("Cannot open ") + argv[4]);
+    f.write(reinterpret_cast<const char*>(x.data()),
+            static_cast<std::streamsize>(sizeof(float) * static_cast<std::size_t>(rows) * cols));
+    if (!f) throw std::runtime_error(std::string("Cannot write ") + argv[4]);
+    return 0;
+}
+
 int cli(int argc, char** argv) {
+    if (argc > 1 && std::string(argv[1]) == "--dump-features") return dump_features(argc, argv);
     const bool verify = argc > 1 && std::string(argv[argc - 1]) == "--verify";
     if (verify) --argc;
     if (argc != 4 && argc != 5 && argc != 6) {
@@ -379,7 +621,16 @@ int cli(int argc, char** argv) {
     }
     const Defined::RowMajorMatrixXf X = features(V, K);
     const CSR_Order sorted = sortCSRByDegree(graph, q);
-    Runner runner(q, sorted, X, K, costs, verify ? &graph : nullptr);
+    // Extension: CWLB_GPUS=N runs every timing loop on GPUs 0..N-1 of this
+    // node; CWLB_DEVICES=a,b,... names the devices instead (one shard each).
+    const std::vector<int> devices = multi_gpu_devices();
+    std::unique_ptr<RunnerBase> runner_p;
+    if (devices.size() > 1) {
+        runner_p.reset(new MultiRunner(devices, graph, X, K, costs, verify));
+    } else {
+        runner_p.reset(new Runner(q, sorted, X, K, costs, verify ? &graph : nullptr));
+    }
+    RunnerBase& runner = *runner_p;
 
     if (candidates) {
         const int cus = q.max_compute_units();

@@ -16,43 +16,25 @@ from __future__ import annotations
 
 
 def shard_bounds(rowoff, edge_weight: float, store_weight: float, world: int, rank: int):
-    """[a, b) of rank `rank` out of `world`: cuts where the prefix sum of
-    edge_weight * deg + store_weight crosses k/world of the total.  Works on a
-    torch tensor or a numpy array of row offsets (int, length rows + 1)."""
+    """[a, b) of rank `rank` out of `world`: the library's cost-balanced cut
+    (cwlb_shard_bounds, the rule the multi-GPU entry points use) of the
+    prefix sum of edge_weight * deg + store_weight at k/world of the total.
+    Takes a torch tensor or a numpy array of row offsets (rows + 1)."""
+    import numpy as np
+
+    import cwlb_spmm as cs
+    try:
+        import torch
+        if isinstance(rowoff, torch.Tensor):
+            rowoff = rowoff.cpu().numpy()
+    except ImportError:  # pragma: no cover
+        pass
     n = len(rowoff) - 1
     if world <= 1:
         return 0, n
-    try:
-        import torch
-        is_torch = isinstance(rowoff, torch.Tensor)
-    except ImportError:  # pragma: no cover
-        is_torch = False
-    if is_torch:
-        import torch
-        deg = (rowoff[1:] - rowoff[:-1]).to(torch.float64)
-        cum = torch.cumsum(deg * edge_weight + store_weight, 0)
-        total = float(cum[-1]) if n else 0.0
-
-        def cut(k):
-            if k <= 0:
-                return 0
-            if k >= world:
-                return n
-            return int(torch.searchsorted(cum, total * k / world).item()) + 1
-    else:
-        import numpy as np
-        deg = np.diff(np.asarray(rowoff, dtype=np.int64)).astype(np.float64)
-        cum = np.cumsum(deg * edge_weight + store_weight)
-        total = float(cum[-1]) if n else 0.0
-
-        def cut(k):
-            if k <= 0:
-                return 0
-            if k >= world:
-                return n
-            return int(np.searchsorted(cum, total * k / world)) + 1
-
-    return min(cut(rank), n), min(cut(rank + 1), n)
+    costs = cs.SpmmCostParams(float(edge_weight), 0.0, float(store_weight), 0.0)
+    b = cs.shard_bounds(np.asarray(rowoff), costs, world)
+    return int(b[rank]), int(b[rank + 1])
 
 
 def shard_csr(rowoff, col, val, a: int, b: int):

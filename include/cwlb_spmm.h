@@ -220,6 +220,80 @@ int cwlb_partition_device_noalloc(void* cuda_stream, int32_t n_rows, const int32
                                   const cwlb_costs* costs, double capacity, cwlb_task* d_tasks,
                                   int64_t max_tasks, int64_t* n_tasks);
 
+/* -------------------------------------------------------------- multi-GPU */
+
+/* The reference runs its whole pipeline on one sycl::queue (main.cpp:514-516):
+ * sortCSRByDegreeDPLCPU (main.cpp:197-278), costWeightedTaskPartitioning
+ * (src/utils.cpp:832-1021) and spmmKernel (src/parallelMatrix.cpp:63-254).
+ * The functions below run that pipeline on several GPUs of one node without
+ * a data exchange: shard s takes a contiguous block of ORIGINAL rows, sorts
+ * and partitions it on its own GPU (the reference's algorithms applied to
+ * the block, so a shard's task list is the partition of its block, not a
+ * slice of the whole graph's), and aggregates it with H replicated; its
+ * output is the block's rows of the original-order result. */
+
+/* Cost-balanced contiguous row shards: bounds[0] = 0, bounds[n_shards] =
+ * n_rows, shard s = original rows [bounds[s], bounds[s+1]).  The cut after
+ * shard s-1 follows the first row whose inclusive prefix sum of the
+ * whole-row weight (Cc + Cl) * deg + Cs (src/utils.cpp:850-852; sequential
+ * float64) reaches total * s / n_shards.  Host code; no device needed. */
+int cwlb_shard_bounds(int32_t n_rows, const int32_t* row_offset, const cwlb_costs* costs,
+                      int32_t n_shards, int32_t* bounds);
+
+typedef struct cwlb_shard cwlb_shard;
+
+/* Builds shard `shard` of `n_shards` on ctx's device from the caller's whole
+ * UNSORTED CSR (host buffers, original row order): cuts the shards as
+ * cwlb_shard_bounds, copies the block's rows to the device, sorts them by
+ * degree, partitions them at `capacity` and checks the task list once; the
+ * result stays resident until cwlb_shard_destroy.  Synchronous.
+ * Errors: CWLB_ERR_RUNTIME when row_offset[n_rows] != nnz (the reference's
+ * message), CWLB_ERR_INVALID_ARGUMENT for bad offsets or shard indices. */
+int cwlb_shard_create(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* row_offset,
+                      const int32_t* col_ind, const float* value, const cwlb_costs* costs,
+                      double capacity, int32_t shard, int32_t n_shards, cwlb_shard** out);
+/* Same, with the whole CSR already in ctx's device memory (one process per
+ * GPU, each holding the graph); the block is sorted straight from it. */
+int cwlb_shard_create_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
+                             const int32_t* d_row_offset, const int32_t* d_col_ind,
+                             const float* d_value, const cwlb_costs* costs, double capacity,
+                             int32_t shard, int32_t n_shards, cwlb_shard** out);
+/* The shard's original rows [*row_begin, *row_end), its nonzeros, task count
+ * and the segment size S the partitioner derived; NULL outputs are skipped. */
+int cwlb_shard_info(const cwlb_shard* shard, int32_t* row_begin, int32_t* row_end, int32_t* nnz,
+                    int64_t* n_tasks, int32_t* segment_size);
+/* Device pointer to the shard's task list (n_tasks entries, indices into the
+ * shard's own degree-sorted rows). */
+int cwlb_shard_tasks(const cwlb_shard* shard, const cwlb_task** d_tasks);
+/* d_out[(r - row_begin) * K + k] = mean aggregation of original row r, for
+ * the shard's rows, with d_H (h_rows x K, row-major, all rows of H) on ctx's
+ * device.  flags: 0 or CWLB_DETERMINISTIC.  Asynchronous on ctx's stream. */
+int cwlb_shard_aggregate_device(cwlb_shard* shard, const float* d_H, int64_t h_rows, int64_t K,
+                                float* d_out, uint32_t flags);
+int cwlb_shard_destroy(cwlb_shard* shard);
+
+/* The whole pipeline over n_gpus contexts (one per GPU, each used by one
+ * host thread that this call starts): from the caller's UNSORTED host CSR
+ * and host H to the host output `out` (n_rows x K, ORIGINAL row order), as
+ * the reference's main.cpp:530-531 + 352-391 computes it on one device.
+ * *time_us receives the largest per-GPU device time of the aggregation
+ * kernels (transfers, sort and partition excluded, as the reference's
+ * kernel time).  Synchronous. */
+int cwlb_spmm_mean_multi(cwlb_ctx* const* ctxs, int32_t n_gpus, int32_t n_rows, int32_t nnz,
+                         const int32_t* row_offset, const int32_t* col_ind, const float* value,
+                         const float* H, int64_t h_rows, int64_t K, const cwlb_costs* costs,
+                         double capacity, float* out, double* time_us);
+
+/* All-gather of a row-sharded matrix across the contexts' GPUs: d_X[g] is a
+ * rows x K row-major buffer on ctxs[g]'s device holding valid rows
+ * [bounds[g], bounds[g+1]) (e.g. the rows that GPU aggregated in a previous
+ * layer); afterwards every buffer holds all rows.  One peer copy per
+ * (source, destination) pair over NVLink, ordered on the contexts' streams:
+ * it starts after the work already queued on every stream, and later work
+ * on any of the streams starts after every copy.  Asynchronous. */
+int cwlb_gather_rows_multi(cwlb_ctx* const* ctxs, int32_t n_gpus, float* const* d_X,
+                           int64_t rows, int64_t K, const int32_t* bounds);
+
 /* ----------------------------------------------------- S-selection helpers */
 
 /* capacity_from_s (main.cpp:281-292). */

@@ -236,3 +236,34 @@ def test_loader_parallel_parse_matches_reference(workdir, reference, damage):
         assert out.split()[2] == f"{h:016x}"
     else:
         assert rc == 1 and err.strip() == str(ei.value)
+
+
+def _dump_cli_features(tmp_path, rows, cols):
+    path = tmp_path / f"x_{rows}x{cols}.bin"
+    p = subprocess.run([CWLB, "--dump-features", str(rows), str(cols), str(path)],
+                       capture_output=True, text=True, timeout=120)
+    assert p.returncode == 0, p.stderr
+    return np.fromfile(path, np.float32).reshape(rows, cols)
+
+
+def test_cli_features_equal_the_reference_bits(tmp_path):
+    """The CLI's X (deterministic_features, main.cpp:324-336: mt19937(42),
+    U[0,1) floats, row-major) bit for bit: against the reference build's
+    digest in the golden fixtures, and, where oracle/_ref exists, against the
+    reference's own function on a larger shape."""
+    import hashlib
+    import json
+    from conftest import GOLDEN
+    with open(os.path.join(GOLDEN, "helpers.json")) as fh:
+        h = json.load(fh)
+    x = _dump_cli_features(tmp_path, 33, 17)
+    assert hashlib.sha256(x.tobytes()).hexdigest() == h["features_33x17_sha256"]
+    assert x.reshape(-1)[:8].tolist() == h["features_33x17_first"]
+    so = _ref_so()
+    if not os.path.exists(so):
+        pytest.skip("oracle/_ref not built: checked against the golden digest only")
+    from oracle import Reference
+    ref = Reference(so)
+    want = ref.features(1000, 96)
+    got = _dump_cli_features(tmp_path, 1000, 96)
+    assert np.array_equal(got.view(np.uint32), np.asarray(want, np.float32).view(np.uint32))

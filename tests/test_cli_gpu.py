@@ -219,3 +219,49 @@ def test_costwrite_writes_cost_file(workdir):
     for v in vals[:4]:
         assert re.fullmatch(r"\d+\.\d{6}", v)
         assert float(v) > 0
+
+
+def _run_env(cmd, cwd, extra_env, stdin=""):
+    env = _env()
+    env.update(extra_env)
+    p = subprocess.run(cmd, cwd=cwd, input=stdin, capture_output=True, text=True, env=env,
+                       timeout=900)
+    return p.returncode, p.stdout, p.stderr
+
+
+@pytest.mark.parametrize("argv", [["g", "16", "--S", "8", "--verify"],
+                                  ["g", "24", "--candidates", "--verify"]])
+def test_cli_multi_gpu_shards_verify_and_keep_the_grammar(workdir, argv):
+    # CWLB_DEVICES=0,0: two shards on one B200 (two contexts, two streams),
+    # the multi-GPU runner's whole path; every run verified against the
+    # float64 device aggregation of the unsorted graph.
+    rc, out, err = _run_env([CWLB, *argv], workdir / "build", {"CWLB_DEVICES": "0,0"})
+    assert rc == 0, err
+    assert out.count("[Verify]") >= 1 and "PASS" in out.upper()
+    assert re.search(r"device=.* x2 K=", out)
+    rc1, out1, err1 = run([CWLB, *argv], workdir / "build")
+    assert rc1 == 0, err1
+    strip = lambda t: [ln for ln in template(t) if not ln.startswith("[Verify]")]  # noqa: E731
+    assert strip(out) == strip(out1)
+
+
+def test_cli_multi_gpu_device_list_errors(workdir):
+    rc, out, err = _run_env([CWLB, "g", "16", "--S", "8"], workdir / "build",
+                            {"CWLB_DEVICES": "0,99"})
+    assert rc == 1 and "CWLB_DEVICES" in err
+
+
+def _gpu_count():
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except ImportError:
+        return 0
+
+
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs two GPUs")
+def test_cli_two_gpus(workdir):
+    rc, out, err = _run_env([CWLB, "g", "16", "--S", "8", "--verify"], workdir / "build",
+                            {"CWLB_GPUS": "2"})
+    assert rc == 0, err
+    assert "[Verify]" in out
