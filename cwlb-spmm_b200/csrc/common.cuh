@@ -97,7 +97,7 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
                       const int32_t* col, const float* val, const int32_t* origin,
                       const float* H, int64_t h_rows, int64_t K, const cwlb_task* tasks,
                       int64_t n_tasks, float* out, uint32_t flags,
-                      const int32_t* sched = nullptr);
+                      const int32_t* sched = nullptr, int64_t n_slots = 0);
 // Copies of caller memory for the host-buffer entry points (staging.cu).
 // copy_to_device is asynchronous on `s`; once it returns, the source may be
 // reused; copy_to_host returns when `dst` holds the data.  Large pageable
@@ -105,6 +105,13 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
 void copy_to_device(cwlb_ctx* ctx, void* dst, const void* src, size_t bytes, cudaStream_t s);
 void copy_to_host(cwlb_ctx* ctx, void* dst, const void* src, size_t bytes, cudaStream_t s);
 void destroy_stager(cwlb_ctx* ctx);
+// Aggregation plans (plan.cu).
+cwlb_plan* plan_create(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
+                       const int32_t* col, const float* val, const cwlb_task* tasks,
+                       int64_t n_tasks, int32_t group_size);
+void plan_aggregate(cwlb_plan* p, const int32_t* origin, const float* H, int64_t h_rows, int64_t K,
+                    float* out, uint32_t flags);
+void plan_destroy(cwlb_plan* p);
 // Writes `count` floats of 1.0f (spmm.cu).
 void launch_fill_ones(cwlb_ctx* ctx, float* dst, size_t count);
 // Float64 reference of the aggregation over an unsorted CSR (spmm.cu).
@@ -117,6 +124,12 @@ void run_tasks_check(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* 
 void launch_sort_by_degree(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                            const int32_t* col, const float* val, int32_t* origin,
                            int32_t* new_rowoff, int32_t* new_col, float* new_val);
+// Stable LSD radix sort of (key, value) pairs by the low `bits` bits of the
+// keys, 8 bits per pass, in place on ctx's stream (reorder.cu); scratch holds
+// radix_sort_pairs_scratch_bytes(n, SM count) bytes.
+size_t radix_sort_pairs_scratch_bytes(int32_t n, int sm_count);
+void radix_sort_pairs(cwlb_ctx* ctx, uint32_t* keys, int32_t* vals, int32_t n, int bits,
+                      void* scratch);
 // Returns the number of tasks; the tasks are in ctx->part_tasks.
 int64_t run_partition(cwlb_ctx* ctx, int32_t n_rows, const int32_t* d_rowoff,
                       const cwlb_costs& costs, double capacity);

@@ -22,6 +22,8 @@
 // The reference's own GPU sorter (src/utils.cpp:106-339) uses an atomic
 // bucket scatter whose tie order is nondeterministic; it is not the parity
 // target.
+#include <algorithm>
+
 #include "common.cuh"
 #include "scan.cuh"
 
@@ -207,6 +209,57 @@ __global__ void __launch_bounds__(kGatherThreads)
 }
 
 }  // namespace
+
+size_t radix_sort_pairs_scratch_bytes(int32_t n, int sm_count) {
+    const int64_t nn = n > 0 ? n : 1;
+    const int rounds = static_cast<int>(std::min<int64_t>(
+        kSortMaxRounds,
+        std::max<int64_t>(1, ceil_div(nn, int64_t{kSortThreads} * 2 * sm_count))));
+    const int64_t n_tiles = ceil_div(nn, int64_t{kSortThreads} * rounds);
+    auto al = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
+    return al(sizeof(uint32_t) * nn) + al(sizeof(int32_t) * nn) +
+           al(sizeof(int32_t) * n_tiles * kRadix) +
+           al(scan_scratch_bytes<int32_t>(n_tiles * kRadix));
+}
+
+void radix_sort_pairs(cwlb_ctx* ctx, uint32_t* keys, int32_t* vals, int32_t n, int bits,
+                      void* scratch) {
+    if (n <= 1 || bits <= 0) return;
+    cudaStream_t s = ctx->stream;
+    const int sm = ctx->props.multiProcessorCount;
+    const int rounds = static_cast<int>(std::min<int64_t>(
+        kSortMaxRounds, std::max<int64_t>(1, ceil_div(n, int64_t{kSortThreads} * 2 * sm))));
+    const int64_t n_tiles = ceil_div(n, int64_t{kSortThreads} * rounds);
+    const int64_t hist_n = n_tiles * kRadix;
+    auto al = [](size_t b) { return (b + 255) & ~static_cast<size_t>(255); };
+    char* p = static_cast<char*>(scratch);
+    uint32_t* keys_b = reinterpret_cast<uint32_t*>(p);
+    int32_t* vals_b = reinterpret_cast<int32_t*>(p + al(sizeof(uint32_t) * n));
+    int32_t* hist = reinterpret_cast<int32_t*>(p + al(sizeof(uint32_t) * n) + al(sizeof(int32_t) * n));
+    void* scan_tmp = p + al(sizeof(uint32_t) * n) + al(sizeof(int32_t) * n) +
+                     al(sizeof(int32_t) * hist_n);
+    uint32_t* kin = keys;
+    uint32_t* kout = keys_b;
+    int32_t* vin = vals;
+    int32_t* vout = vals_b;
+    const int passes = (bits + 7) / 8;
+    for (int pass = 0; pass < passes; ++pass) {
+        const int shift = 8 * pass;
+        radix_hist_kernel<<<static_cast<unsigned>(n_tiles), kSortThreads, 0, s>>>(
+            kin, n, shift, rounds, n_tiles, hist);
+        CWLB_LAUNCH_CHECK("radix_hist_kernel");
+        device_exclusive_scan<int32_t>(hist, hist, hist_n, scan_tmp, s);
+        radix_scatter_kernel<<<static_cast<unsigned>(n_tiles), kSortThreads, 0, s>>>(
+            kin, vin, n, shift, rounds, n_tiles, hist, kout, vout);
+        CWLB_LAUNCH_CHECK("radix_scatter_kernel");
+        std::swap(kin, kout);
+        std::swap(vin, vout);
+    }
+    if (kin != keys) {
+        CWLB_CUDA(cudaMemcpyAsync(keys, kin, sizeof(uint32_t) * n, cudaMemcpyDeviceToDevice, s));
+        CWLB_CUDA(cudaMemcpyAsync(vals, vin, sizeof(int32_t) * n, cudaMemcpyDeviceToDevice, s));
+    }
+}
 
 void launch_sort_by_degree(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                            const int32_t* col, const float* val, int32_t* origin,

@@ -66,9 +66,10 @@ struct SpmmArgs {
     // last) instead of atomics.  nullptr: atomic mode.
     float* __restrict__ frag;
     const int32_t* __restrict__ frag_pos;
-    // Optional launch order: warp slot i runs task sched[i] (a permutation of
-    // [0, n_tasks)); nullptr runs task i.
+    // Optional launch order: warp slot i (i < n_slots) runs task sched[i], an
+    // index into [0, n_tasks); nullptr runs task i for every i < n_tasks.
     const int32_t* __restrict__ sched;
+    int64_t n_slots;
 };
 
 __device__ __forceinline__ void raise_err(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
@@ -342,7 +343,7 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
     constexpr int G = VecCfg<L, V>::G;
     const int lane = threadIdx.x & 31;
     const int64_t slot = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
-    if (slot >= a.n_tasks) return;
+    if (slot >= a.n_slots) return;
     const int64_t t = a.sched ? static_cast<int64_t>(__ldg(a.sched + slot)) : slot;
     if (t < 0 || t >= a.n_tasks) {  // an order entry outside the task list
         if ((threadIdx.x & 31) == 0) raise_err(a.err, CWLB_DEVERR_ROW_RANGE);
@@ -735,7 +736,7 @@ template <int L, int V>
 void launch_vec(const SpmmArgs& a, bool stage, cudaStream_t s) {
     const int64_t K4 = a.K >> 2;
     const int64_t tiles = ceil_div(K4, L * V);
-    dim3 grid(static_cast<unsigned>(ceil_div(a.n_tasks, kWarpsPerCta)),
+    dim3 grid(static_cast<unsigned>(ceil_div(a.n_slots, kWarpsPerCta)),
               static_cast<unsigned>(tiles));
     if (stage) {
         spmm_vec_kernel<L, V, true><<<grid, kThreads, 0, s>>>(a);
@@ -789,7 +790,8 @@ void pick_vec_shape(int64_t K4, int& L, int& V) {
 void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                       const int32_t* col, const float* val, const int32_t* origin,
                       const float* H, int64_t h_rows, int64_t K, const cwlb_task* tasks,
-                      int64_t n_tasks, float* out, uint32_t flags, const int32_t* sched) {
+                      int64_t n_tasks, float* out, uint32_t flags, const int32_t* sched,
+                      int64_t n_slots) {
     if (K <= 0 || n_rows <= 0) return;
     cudaStream_t s = ctx->stream;
     const bool covered = (flags & CWLB_ROWS_COVERED) != 0;
@@ -815,6 +817,7 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
     a.nnz = nnz;
     a.write_empty = covered ? 1 : 0;
     a.sched = sched;
+    a.n_slots = sched ? n_slots : n_tasks;
 
     if (covered) {
         dim3 grid(static_cast<unsigned>(ceil_div(n_tasks, kThreads)));
@@ -858,6 +861,10 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
 
     const bool aligned = (reinterpret_cast<uintptr_t>(H) % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(out) % 16 == 0) && (K % 4 == 0);
+    if (sched && (!aligned || det)) {
+        fail(CWLB_ERR_RUNTIME, "internal: a launch order needs the vector kernel, atomic mode");
+    }
+    if (a.n_slots <= 0) return;
     if (aligned) {
         int L = 32, V = 1;
         pick_vec_shape(K >> 2, L, V);

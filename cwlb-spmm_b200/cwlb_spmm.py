@@ -126,6 +126,11 @@ _sig("cwlb_shard_destroy", [_vp])
 _sig("cwlb_spmm_mean_multi", [C.POINTER(_vp), _i32, _i32, _i32, _vp, _vp, _vp, _vp, _i64, _i64,
                               C.POINTER(cwlb_costs), _dbl, _vp, C.POINTER(_dbl)])
 _sig("cwlb_gather_rows_multi", [C.POINTER(_vp), _i32, C.POINTER(_vp), _i64, _i64, _vp])
+_sig("cwlb_plan_create", [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _i64, _i32, C.POINTER(_vp)])
+_sig("cwlb_plan_info", [_vp, C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i32),
+                        C.POINTER(_u32)])
+_sig("cwlb_plan_aggregate_device", [_vp, _vp, _vp, _i64, _i64, _vp, _u32])
+_sig("cwlb_plan_destroy", [_vp])
 _sig("cwlb_validate_result", [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _i64,
                               _i64, C.c_float, C.POINTER(_i32)])
 
@@ -379,6 +384,50 @@ class Context:
         _check(_lib.cwlb_tasks_check(self._h, n_rows, nnz, d_rowoff, d_tasks, n_tasks,
                                      C.byref(bad), C.byref(unc), C.byref(nz)))
         return dict(bad_tasks=bad.value, uncovered_rows=unc.value, nnz_coverage_errors=nz.value)
+
+
+# ---------------------------------------------------------------------------
+# aggregation plans (a task list prepared once for many launches)
+
+PLAN_DISABLED, PLAN_FEW_FRAGMENTS, PLAN_VALUES, PLAN_UNSORTED, PLAN_NO_REUSE = 1, 2, 4, 8, 16
+
+
+class Plan:
+    """cwlb_plan: a reordered CSR's task list prepared once (single-row
+    fragment tasks of neighbouring rows grouped, their column unions merged)
+    for repeated aggregations.  The device pointers passed in must stay valid
+    and unchanged while the plan lives."""
+
+    def __init__(self, ctx: "Context", n_rows, nnz, d_rowoff, d_col, d_val, d_tasks, n_tasks,
+                 group_size=0):
+        h = _vp()
+        _check(_lib.cwlb_plan_create(ctx.handle, n_rows, nnz, d_rowoff, d_col, d_val, d_tasks,
+                                     n_tasks, group_size, C.byref(h)))
+        self._h = h
+        self.ctx = ctx
+
+    def info(self) -> dict:
+        gt, gn, ue, gs, why = _i64(), _i64(), _i64(), _i32(), _u32()
+        _check(_lib.cwlb_plan_info(self._h, C.byref(gt), C.byref(gn), C.byref(ue), C.byref(gs),
+                                   C.byref(why)))
+        return dict(grouped_tasks=gt.value, grouped_nnz=gn.value, union_entries=ue.value,
+                    group_size=gs.value, off_reason=why.value)
+
+    def aggregate_device(self, d_origin, d_H, h_rows, K, d_out, flags=0):
+        """One aggregation (cwlb_spmm_mean_device's flags), asynchronous on
+        the context's stream."""
+        _check(_lib.cwlb_plan_aggregate_device(self._h, d_origin, d_H, h_rows, K, d_out, flags))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.cwlb_plan_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 # ---------------------------------------------------------------------------

@@ -149,6 +149,45 @@ int cwlb_spmm_mean_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
                           int64_t h_rows, int64_t K, const cwlb_task* d_tasks, int64_t n_tasks,
                           float* d_out, uint32_t flags);
 
+/* Aggregation plan: a task list prepared once for many launches (the
+ * reference's 70-launch timing loop, main.cpp:372-406, or one graph layer
+ * after another); no counterpart in the reference.  Same results as
+ * cwlb_spmm_mean_device on the same inputs: every task covers exactly its
+ * own nonzeros and is written as the task kernel writes it; only the order
+ * of additions inside a row fragment may differ (within the same tolerance),
+ * and rows that one task covers whole are computed by the task kernel.
+ * Building (synchronous) groups single-row fragment tasks of neighbouring
+ * rows, `group_size` per group (0: the library's choice, 8; 2-4: 4; 5-8: 8;
+ * 1: no groups), and stores each group's merged union of nonzeros in runs of
+ * equal member mask; one warp then aggregates a group, loading each distinct
+ * H row once, summing a run in registers and adding the sum to the run's
+ * members.  Groups are kept only when every grouped value is 1.0f, every
+ * grouped fragment's columns are non-decreasing and the union saves enough
+ * loads; otherwise (and, per call, for K not in {32, 64, 128}, unaligned H or
+ * out, or CWLB_DETERMINISTIC) the plan runs the task kernel over all tasks,
+ * and cwlb_plan_info's *off_reason says why (CWLB_PLAN_* bits).  The plan
+ * keeps the CSR and task pointers: they must stay valid and unchanged until
+ * cwlb_plan_destroy.  Its own buffers are device memory it allocates. */
+#define CWLB_PLAN_DISABLED 1u       /* group_size 1 */
+#define CWLB_PLAN_FEW_FRAGMENTS 2u  /* too few single-row fragment tasks */
+#define CWLB_PLAN_VALUES 4u         /* a grouped value is not 1.0f */
+#define CWLB_PLAN_UNSORTED 8u       /* a grouped fragment's columns decrease */
+#define CWLB_PLAN_NO_REUSE 16u      /* the union would save too few loads */
+typedef struct cwlb_plan cwlb_plan;
+int cwlb_plan_create(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* d_row_offset,
+                     const int32_t* d_col_ind, const float* d_value, const cwlb_task* d_tasks,
+                     int64_t n_tasks, int32_t group_size, cwlb_plan** out);
+/* Tasks in groups, their nonzeros, the union entries that replace them, the
+ * group size in use (0: none) and the CWLB_PLAN_* reasons groups are off. */
+int cwlb_plan_info(const cwlb_plan* plan, int64_t* grouped_tasks, int64_t* grouped_nnz,
+                   int64_t* union_entries, int32_t* group_size, uint32_t* off_reason);
+/* One aggregation with cwlb_spmm_mean_device's contract (out zero-filled
+ * first, or CWLB_ROWS_COVERED / CWLB_DETERMINISTIC as there), asynchronous
+ * on the plan's context stream. */
+int cwlb_plan_aggregate_device(cwlb_plan* plan, const int32_t* d_origin_local, const float* d_H,
+                               int64_t h_rows, int64_t K, float* d_out, uint32_t flags);
+int cwlb_plan_destroy(cwlb_plan* plan);
+
 /* Validates a device task list against a reordered CSR (no counterpart in the
  * reference, which trusts its partitioner): *bad_tasks counts tasks whose rows
  * fall outside [0, n_rows); *uncovered_rows counts rows in no task's row
