@@ -332,6 +332,8 @@ int cwlb_ctx_create(int device, cwlb_ctx** out) {
             CWLB_CUDA(cudaEventCreate(&ctx->ev_start));
             CWLB_CUDA(cudaEventCreate(&ctx->ev_stop));
             CWLB_CUDA(cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking));
+            CWLB_CUDA(cudaEventCreateWithFlags(&ctx->plan_fork, cudaEventDisableTiming));
+            CWLB_CUDA(cudaEventCreateWithFlags(&ctx->plan_join, cudaEventDisableTiming));
             for (int c = 0; c < cwlb_ctx::kPipeChunks; ++c) {
                 CWLB_CUDA(cudaEventCreateWithFlags(&ctx->pipe_ready[c], cudaEventDisableTiming));
                 CWLB_CUDA(cudaEventCreate(&ctx->pipe_t0[c]));
@@ -361,6 +363,8 @@ int cwlb_ctx_destroy(cwlb_ctx* ctx) {
         if (ctx->d_error_flags) cudaFree(ctx->d_error_flags);
         if (ctx->copy_stream) cudaStreamSynchronize(ctx->copy_stream);
         if (ctx->ev_start) cudaEventDestroy(ctx->ev_start);
+        if (ctx->plan_fork) cudaEventDestroy(ctx->plan_fork);
+        if (ctx->plan_join) cudaEventDestroy(ctx->plan_join);
         if (ctx->ev_stop) cudaEventDestroy(ctx->ev_stop);
         for (int c = 0; c < cwlb_ctx::kPipeChunks; ++c) {
             if (ctx->pipe_ready[c]) cudaEventDestroy(ctx->pipe_ready[c]);

@@ -71,6 +71,8 @@ struct cwlb_ctx {
     // aggregating each chunk's tasks on `stream` as soon as it has arrived.
     static constexpr int kPipeChunks = 8;
     cudaStream_t copy_stream = nullptr;
+    // A plan's groups run on copy_stream beside the ungrouped tasks.
+    cudaEvent_t plan_fork = nullptr, plan_join = nullptr;
     cudaEvent_t pipe_ready[kPipeChunks] = {};
     cudaEvent_t pipe_t0[kPipeChunks] = {}, pipe_t1[kPipeChunks] = {};
     uint32_t* d_error_flags = nullptr;  // CWLB_DEVERR_* bits raised by kernels
@@ -91,6 +93,9 @@ namespace cwlb {
 
 // launch_spmm_mean flag (internal): the caller has already zeroed `out`.
 constexpr uint32_t kFlagOutCleared = 1u << 31;
+// launch_spmm_mean flag (internal): the split rows of a CWLB_ROWS_COVERED call
+// have already been zeroed (by an earlier call with n_slots == 0).
+constexpr uint32_t kFlagSplitZeroed = 1u << 30;
 
 // Launchers implemented in the .cu files (all asynchronous on ctx->stream).
 void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,

@@ -10,7 +10,7 @@
 // columns): on the R-MAT configuration 2 graph, 8 such fragments reference
 // about 0.6 distinct columns per nonzero.
 //
-// A plan therefore GROUPS single-row fragment tasks, R = 8 (or 4) per group,
+// A plan therefore GROUPS single-row fragment tasks, R = 4 (or 8) per group,
 // taken from blocks of kRowBlock consecutive rows in order of their first
 // column, and stores each group's merged union of nonzeros bucketed by the
 // MASK of members holding each column: runs of equal mask, columns ascending
@@ -336,6 +336,11 @@ __global__ void __launch_bounds__(kPlanThreads)
 // ---------------------------------------------------------------------------
 // The group kernel.
 
+#ifndef CWLB_GROUP_MIN_BLOCKS
+#define CWLB_GROUP_MIN_BLOCKS 2
+#endif
+constexpr int kGroupMinBlocks = CWLB_GROUP_MIN_BLOCKS;  // CTAs per SM the registers allow
+
 template <int VW>
 struct VecT;
 template <>
@@ -428,13 +433,16 @@ __device__ __forceinline__ void add_member(T (&acc)[R], int b, const T& x) {
 // flight.  The group's entries come as runs of equal member mask: a run's H
 // rows are summed into s, and s is added to each of the run's members once.
 template <int VW, int R, int U>
-__global__ void __launch_bounds__(kPlanThreads) group_kernel(GroupArgs a) {
+__global__ void __launch_bounds__(kPlanThreads, kGroupMinBlocks) group_kernel(GroupArgs a) {
     using V = VecT<VW>;
     using T = typename V::T;
     constexpr int kBins = 1 << R;
     const int lane = threadIdx.x & 31;
-    const int64_t g = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    if (g >= a.n_groups) return;
+    // Groups run heaviest first: they are stored in ascending row (degree)
+    // order, and the hub groups at the end hold the most entries.
+    const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (w >= a.n_groups) return;
+    const int64_t g = a.n_groups - 1 - w;
 
     // Lane m < R describes member m (its row's origin and degree).
     int32_t m_orig = 0;
@@ -486,6 +494,7 @@ __global__ void __launch_bounds__(kPlanThreads) group_kernel(GroupArgs a) {
                 my_col = static_cast<uint32_t>(c);
             }
         }
+        const bool chunk_ok = !__any_sync(0xffffffffu, my_col >> 31);
         for (int32_t j = 0; j < cnt; j += U) {
             uint32_t cj[U];
             T x[U];
@@ -494,6 +503,18 @@ __global__ void __launch_bounds__(kPlanThreads) group_kernel(GroupArgs a) {
 #pragma unroll
             for (int u = 0; u < U; ++u)
                 x[u] = V::load(Hv + static_cast<size_t>(cj[u] & 0x7fffffffu) * 32 + lane);
+            if (chunk_ok && j + U <= cnt && run_left > U) {
+                // The whole step lies inside the current run: sum it as a
+                // tree (short dependency chains) and skip the bookkeeping.
+#pragma unroll
+                for (int w = 1; w < U; w <<= 1) {
+#pragma unroll
+                    for (int u = 0; u + w < U; u += 2 * w) V::add(x[u], x[u + w]);
+                }
+                V::add(s, x[0]);
+                run_left -= U;
+                continue;
+            }
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 if (j + u >= cnt) break;
@@ -533,14 +554,7 @@ __global__ void __launch_bounds__(kPlanThreads) group_kernel(GroupArgs a) {
 template <int VW, int R>
 void launch_group(const GroupArgs& a, cudaStream_t s) {
     const unsigned grid = static_cast<unsigned>(ceil_div(a.n_groups, kPlanThreads / 32));
-    const char* u = std::getenv("CWLB_GROUP_U");  // tuning experiment only
-    if (u && std::atoi(u) == 8) {
-        group_kernel<VW, R, 8><<<grid, kPlanThreads, 0, s>>>(a);
-    } else if (u && std::atoi(u) == 2) {
-        group_kernel<VW, R, 2><<<grid, kPlanThreads, 0, s>>>(a);
-    } else {
-        group_kernel<VW, R, 4><<<grid, kPlanThreads, 0, s>>>(a);
-    }
+    group_kernel<VW, R, 4><<<grid, kPlanThreads, 0, s>>>(a);
     CWLB_LAUNCH_CHECK("group_kernel");
 }
 
@@ -681,10 +695,20 @@ void plan_aggregate(cwlb_plan* p, const int32_t* origin, const float* H, int64_t
         return;
     }
     if (p->nnz > 0 && h_rows <= 0) fail(CWLB_ERR_INVALID_ARGUMENT, "H has no rows but the CSR has nonzeros");
-    // The zero-fill (or the split-row zeroing) over all tasks and the
-    // ungrouped tasks first; then the groups add into the same rows.
+    // 1. The zero-fill (or the split-row zeroing) over all tasks.
+    // 2. The ungrouped tasks on the context's stream and the groups on its
+    //    second stream, concurrently: rows that a task covers whole, and
+    //    empty rows, are written only by ungrouped tasks; rows split between
+    //    tasks only receive atomic adds after step 1.
+    // 3. The context's stream waits for the groups.
+    const int32_t* rest = p->rest.as<int32_t>(1);
     launch_spmm_mean(ctx, p->n_rows, p->nnz, p->rowoff, p->col, p->val, origin, H, h_rows, K,
-                     p->tasks, p->n_tasks, out, flags, p->rest.as<int32_t>(1), p->n_rest);
+                     p->tasks, p->n_tasks, out, flags, rest, 0);
+    CWLB_CUDA(cudaEventRecord(ctx->plan_fork, ctx->stream));
+    CWLB_CUDA(cudaStreamWaitEvent(ctx->copy_stream, ctx->plan_fork, 0));
+    launch_spmm_mean(ctx, p->n_rows, p->nnz, p->rowoff, p->col, p->val, origin, H, h_rows, K,
+                     p->tasks, p->n_tasks, out, flags | kFlagOutCleared | kFlagSplitZeroed, rest,
+                     p->n_rest);
     GroupArgs a{};
     a.rowoff = p->rowoff;
     a.origin = origin;
@@ -703,10 +727,12 @@ void plan_aggregate(cwlb_plan* p, const int32_t* origin, const float* H, int64_t
     a.n_rows = p->n_rows;
     a.nnz = p->nnz;
     switch (K) {
-        case 32: launch_group_r<1>(p->R, a, ctx->stream); break;
-        case 64: launch_group_r<2>(p->R, a, ctx->stream); break;
-        default: launch_group_r<4>(p->R, a, ctx->stream); break;
+        case 32: launch_group_r<1>(p->R, a, ctx->copy_stream); break;
+        case 64: launch_group_r<2>(p->R, a, ctx->copy_stream); break;
+        default: launch_group_r<4>(p->R, a, ctx->copy_stream); break;
     }
+    CWLB_CUDA(cudaEventRecord(ctx->plan_join, ctx->copy_stream));
+    CWLB_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->plan_join, 0));
 }
 
 cwlb_plan* plan_create(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
@@ -724,7 +750,7 @@ cwlb_plan* plan_create(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t
     p->n_tasks = n_tasks;
     p->n_rest = n_tasks;
     try {
-        if (group_size == 0) group_size = 8;
+        if (group_size == 0) group_size = 4;  // measured faster than 8 on B200
         if (group_size <= 1) {
             p->off_reason |= CWLB_PLAN_DISABLED;
         } else {

@@ -819,7 +819,7 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
     a.sched = sched;
     a.n_slots = sched ? n_slots : n_tasks;
 
-    if (covered) {
+    if (covered && !(flags & kFlagSplitZeroed)) {
         dim3 grid(static_cast<unsigned>(ceil_div(n_tasks, kThreads)));
         zero_split_rows_kernel<<<grid, kThreads, 0, s>>>(a);
         CWLB_LAUNCH_CHECK("zero_split_rows_kernel");

@@ -224,6 +224,13 @@ def normal_features_torch(rows, cols, seed, device="cuda"):
 
 # ---------------------------------------------------------------------------
 # the benchmark configurations
+#
+# S: the segment size both bench arms (the GPU path and the CPU reference
+# arm) partition with, so that they time the same task list.  Configurations
+# 2-5 use the third candidate of the reference's --candidates procedure
+# (wave_based_s with the nnz-keyed w table, main.cpp:87-95 and 295-321, at
+# w = 2048 and 148 SMs), the candidate that procedure keeps on a B200 (for
+# configuration 2, S = 181 times within 1% of it).
 
 CONFIGS = {
     1: dict(name="er4096_k32", graph=("er", dict(n=4096, avg_degree=8, seed=0)),
@@ -233,15 +240,15 @@ CONFIGS = {
     2: dict(name="rmat18_k128", graph=("rmat", dict(scale=18, n_edges=85_000_000, a=0.57,
                                                      b=0.19, c=0.19, seed=1, symmetrize=True,
                                                      drop_self_loops=True, dedupe=True)),
-            K=128, features=("uniform", 1), S=None),
+            K=128, features=("uniform", 1), S=362),
     3: dict(name="poisson2.4m_k512", graph=("poisson", dict(n=2_400_000, mean=51, seed=2)),
-            K=512, features=("normal", 2), S=None),
+            K=512, features=("normal", 2), S=404),
     4: dict(name="geom16m_k32", graph=("geometric", dict(n=1 << 24, mean=4, max_degree=200,
                                                           seed=3)),
-            K=32, features=("uniform", 3), S=None),
+            K=32, features=("uniform", 3), S=222),
     5: dict(name="rmat22_k64", graph=("rmat", dict(scale=22, n_edges=1 << 28, a=0.70, b=0.10,
                                                     c=0.10, seed=4)),
-            K=64, features=("uniform", 4), S=None),
+            K=64, features=("uniform", 4), S=886),
 }
 
 

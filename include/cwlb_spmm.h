@@ -157,7 +157,7 @@ int cwlb_spmm_mean_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
  * of additions inside a row fragment may differ (within the same tolerance),
  * and rows that one task covers whole are computed by the task kernel.
  * Building (synchronous) groups single-row fragment tasks of neighbouring
- * rows, `group_size` per group (0: the library's choice, 8; 2-4: 4; 5-8: 8;
+ * rows, `group_size` per group (0: the library's choice, 4; 2-4: 4; 5-8: 8;
  * 1: no groups), and stores each group's merged union of nonzeros in runs of
  * equal member mask; one warp then aggregates a group, loading each distinct
  * H row once, summing a run in registers and adding the sum to the run's

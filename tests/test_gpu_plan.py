@@ -115,7 +115,7 @@ def test_grouped_plan_matches_oracle(ctx, oracle, K, gs):
 def test_plan_matches_the_task_kernel(ctx, oracle):
     case = _Case(ctx, oracle, *_sorted_graph(oracle, seed=53), S=64, K=128)
     plan = case.plan()
-    assert plan.info()["group_size"] == 8
+    assert plan.info()["group_size"] == 4  # the default
     out_p = case.run(plan, cs.ROWS_COVERED)
     out_t = torch.full_like(out_p, float("nan"))
     ctx.spmm_mean_device(case.n, case.nnz, case.d["sro"].data_ptr(), case.d["scol"].data_ptr(),
@@ -158,7 +158,7 @@ def test_plan_fallbacks_report_why_and_match(ctx, oracle, kind, reason):
 def test_plan_per_call_fallbacks_match(ctx, oracle):
     case = _Case(ctx, oracle, *_sorted_graph(oracle, seed=54), S=40, K=96)
     plan = case.plan()
-    assert plan.info()["group_size"] == 8  # built; K = 96 runs the task kernel
+    assert plan.info()["group_size"] == 4  # built; K = 96 runs the task kernel
     case.check(case.run(plan, cs.ROWS_COVERED), "K=96")
     # Deterministic merge: the task kernel's fixed order, bit-identical twice.
     a = case.run(plan, cs.ROWS_COVERED | cs.DETERMINISTIC).cpu().numpy()
@@ -178,7 +178,7 @@ def test_plan_honours_a_partial_task_list(ctx, oracle):
     part = np.ascontiguousarray(tasks[::3])  # every third task only
     case = _Case(ctx, oracle, origin, sro, scol, sval, S=40, K=128, tasks=part)
     plan = case.plan()
-    assert plan.info()["group_size"] == 8
+    assert plan.info()["group_size"] == 4  # the default
     out = case.run(plan, 0)
     want = oracle.spmm_mean(sro, scol, sval, origin, case.X, part)
     err = np.abs(out.cpu().numpy() - want).max()
@@ -189,7 +189,7 @@ def test_plan_honours_a_partial_task_list(ctx, oracle):
 def test_plan_column_outside_h_raises_the_device_flag(ctx, oracle):
     case = _Case(ctx, oracle, *_sorted_graph(oracle, seed=56), S=40, K=64)
     plan = case.plan()
-    assert plan.info()["group_size"] == 8
+    assert plan.info()["group_size"] == 4  # the default
     short = case.d_X[: case.n // 2].contiguous()  # H without its upper half
     out = torch.zeros((case.n, 64), device="cuda")
     plan.aggregate_device(case.d["org"].data_ptr(), short.data_ptr(), short.shape[0], 64,
