@@ -60,7 +60,9 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=2,
                     help="benchmark configuration (1-5, graphs.CONFIGS)")
-    ap.add_argument("--S", type=int, default=0, help="segment size; 0 = candidate search")
+    ap.add_argument("--S", type=int, default=-1,
+                    help="segment size; -1 = the configuration's S (graphs.CONFIGS, the same "
+                         "for both arms), 0 = the reference's --candidates search (GPU arm)")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target CPU time of the CPU-baseline sample")
@@ -536,7 +538,7 @@ def run_ours(args):
     cus = ctx.device_info()["max_compute_units"]
     if args.S > 0:
         candidates = [args.S]
-    elif cfg["S"]:
+    elif args.S < 0 and cfg["S"]:
         candidates = [cfg["S"]]
     else:
         ws = cs.recommended_candidate_w(wl["nnz_total"])
