@@ -72,6 +72,10 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--deterministic", action="store_true",
                     help="merge split rows in a fixed order (CWLB_DETERMINISTIC)")
+    ap.add_argument("--plan", type=int, default=-1, metavar="GROUP_SIZE",
+                    help="N = 1: time an aggregation plan (cwlb_plan_*, built outside the timed "
+                         "region) with this group size (0 = the library's choice) instead of "
+                         "the task kernel")
     ap.add_argument("--x-sharded", action="store_true",
                     help="N > 1: X arrives row-sharded (as a prior layer leaves it); every "
                          "step all-gathers it over NCCL before the aggregation")
@@ -296,12 +300,13 @@ def _scan_launches(n):
     return 1 if n <= 4096 else 2 + _scan_launches(-(-n // 4096))
 
 
-def launches_per_step(flags, n_tasks):
+def launches_per_step(flags, n_tasks, plan_groups=False):
     """Kernels of this library per aggregation step: the zero pre-pass
-    (rows-covered mode), the aggregation, and in deterministic mode the
-    fragment plan (count, scan, place) and merge (window, final)."""
+    (rows-covered mode), the aggregation (plus the group kernel when a plan
+    with groups runs), and in deterministic mode the fragment plan (count,
+    scan, place) and merge (window, final)."""
     import cwlb_spmm as cs
-    n = 1 + (1 if flags & cs.ROWS_COVERED else 0)
+    n = 1 + (1 if flags & cs.ROWS_COVERED else 0) + (1 if plan_groups else 0)
     if flags & cs.DETERMINISTIC:
         n += 4 + _scan_launches(n_tasks)
     return n
@@ -325,6 +330,10 @@ def run_step(ctx, wl, tasks, n_tasks, out, flags):
     if wl.get("shard") is not None:
         wl["shard"].aggregate_device(wl["X"].data_ptr(), wl["X"].shape[0], wl["K"],
                                      out.data_ptr(), flags & 2)  # DETERMINISTIC only
+        return
+    if wl.get("plan") is not None:
+        wl["plan"].aggregate_device(wl["org"].data_ptr(), wl["X"].data_ptr(), wl["X"].shape[0],
+                                    wl["K"], out.data_ptr(), flags)
         return
     ctx.spmm_mean_device(wl["n"], wl["nnz"], wl["sro"].data_ptr(), wl["scol"].data_ptr(),
                          wl["sval"].data_ptr(), wl["org"].data_ptr(), wl["X"].data_ptr(),
@@ -577,6 +586,15 @@ def run_ours(args):
         wl["shard"] = make_shard(ctx, wl, costs, S, rank, world)
         # The shard's task list is the partition of the same block.
         assert wl["shard"].n_tasks == n_tasks, "shard task count differs"
+    plan_info = None
+    if args.plan >= 0 and world == 1:
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        wl["plan"] = cs.Plan(ctx, wl["n"], wl["nnz"], wl["sro"].data_ptr(), wl["scol"].data_ptr(),
+                             wl["sval"].data_ptr(), tasks.data_ptr(), n_tasks, args.plan)
+        torch.cuda.synchronize()
+        plan_info = wl["plan"].info()
+        plan_info["build_ms"] = round((time.perf_counter() - t0) * 1e3, 3)
 
     for _ in range(args.warmup):
         run_step(ctx, wl, tasks, n_tasks, out, flags)
@@ -711,6 +729,9 @@ def run_ours(args):
                        "process_group_world_size": pg_world,
                        "ms_per_step_by_rank": per_rank_ms,
                        "split_row_merge": "deterministic" if args.deterministic else "atomic",
+                       "aggregation": ("plan (cwlb_plan_aggregate_device): " + json.dumps(plan_info)
+                                       if plan_info else "task kernel (cwlb_spmm_mean_device)"
+                                       if world == 1 else "shards (cwlb_shard_aggregate_device)"),
                        "x": ("row-sharded; one NCCL all-gather per step, inside the timing"
                              if wl.get("x_sharded") else "replicated"),
                        "l2": "inputs larger than L2 (CSR + X > 126 MB), no flush",
@@ -733,14 +754,16 @@ def run_ours(args):
             "e2e": e2e,
             "e2e_weighted": e2e_weighted,
             "parity": parity,
-            "gpu_launches": launches_per_step(flags, n_tasks) * args.steps,
+            "gpu_launches": launches_per_step(
+                flags, n_tasks, bool(plan_info and plan_info["group_size"] > 0)) * args.steps,
             "clocks": clocks,
         }
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
-    if wl.get("shard") is not None:
-        wl["shard"].close()
+    for k in ("shard", "plan"):
+        if wl.get(k) is not None:
+            wl[k].close()
     ctx.close()
     if world > 1:
         import torch.distributed as dist
