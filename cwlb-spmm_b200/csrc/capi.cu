@@ -196,15 +196,8 @@ void spmm_host_staged(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
             copy_h2d(ctx, d_col + nnz_cut[c], col_ind + nnz_cut[c], nnz_cut[c + 1] - nnz_cut[c], cs);
             CWLB_CUDA(cudaEventRecord(ctx->pipe_ready[c], cs));
         }
-        const float* d_val = nullptr;
-        if (unit.get()) {
-            if (ctx->ones_count < static_cast<size_t>(nnz)) {
-                float* d = ctx->ones.as<float>(static_cast<size_t>(nnz));
-                cwlb::launch_fill_ones(ctx, d, static_cast<size_t>(nnz));
-                ctx->ones_count = static_cast<size_t>(nnz);
-            }
-            d_val = static_cast<const float*>(ctx->ones.ptr);
-        } else {
+        const float* d_val = nullptr;  // all values 1.0: the kernels read none
+        if (!unit.get()) {
             float* dv = ctx->in_val.as<float>(static_cast<size_t>(nnz));
             for (int c = 0; c < n_chunks; ++c) {
                 copy_h2d(ctx, dv + nnz_cut[c], value + nnz_cut[c], nnz_cut[c + 1] - nnz_cut[c], cs);
@@ -358,7 +351,7 @@ int cwlb_ctx_destroy(cwlb_ctx* ctx) {
         for (cwlb::DeviceBuffer* b : {&ctx->in_rowoff, &ctx->in_col, &ctx->in_val, &ctx->in_origin,
                                       &ctx->in_H, &ctx->in_tasks, &ctx->out_buf, &ctx->sort_scratch,
                                       &ctx->part_scratch, &ctx->part_desc, &ctx->part_tasks,
-                                      &ctx->check_scratch, &ctx->ones, &ctx->det_scratch})
+                                      &ctx->check_scratch, &ctx->det_scratch})
             b->release();
         if (ctx->d_error_flags) cudaFree(ctx->d_error_flags);
         if (ctx->copy_stream) cudaStreamSynchronize(ctx->copy_stream);

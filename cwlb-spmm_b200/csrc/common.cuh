@@ -80,9 +80,6 @@ struct cwlb_ctx {
     // device) and for the sort / partition pipelines.
     cwlb::DeviceBuffer in_rowoff, in_col, in_val, in_origin, in_H, in_tasks, out_buf;
     cwlb::DeviceBuffer sort_scratch, part_scratch, part_desc, part_tasks, check_scratch;
-    // 1.0f values for host-buffer calls whose values are all one (not copied).
-    cwlb::DeviceBuffer ones;
-    size_t ones_count = 0;
     // Fragment partials and their plan (CWLB_DETERMINISTIC).
     cwlb::DeviceBuffer det_scratch;
     // Created by the first large copy of pageable caller memory.
@@ -117,8 +114,10 @@ cwlb_plan* plan_create(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t
 void plan_aggregate(cwlb_plan* p, const int32_t* origin, const float* H, int64_t h_rows, int64_t K,
                     float* out, uint32_t flags);
 void plan_destroy(cwlb_plan* p);
-// Writes `count` floats of 1.0f (spmm.cu).
-void launch_fill_ones(cwlb_ctx* ctx, float* dst, size_t count);
+// True when every one of the `count` device floats is exactly 1.0f
+// (synchronous; d_flag is one word of device scratch) (spmm.cu).  Kernels
+// given NULL values treat every value as 1.0f.
+bool values_all_one(cwlb_ctx* ctx, const float* d_val, size_t count, unsigned int* d_flag);
 // Float64 reference of the aggregation over an unsorted CSR (spmm.cu).
 void launch_spmm_mean_reference(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                                 const int32_t* col, const float* val, const float* H,

@@ -36,6 +36,7 @@ struct cwlb_shard {
     int32_t segment = 0;                 // S the partitioner derived
     int64_t n_tasks = 0;
     uint32_t flags = 0;                  // CWLB_ROWS_COVERED once checked
+    bool unit = false;                   // every value is 1.0: kernels read none
     cwlb::DeviceBuffer origin, rowoff, col, val, tasks;
 };
 
@@ -120,6 +121,11 @@ void build_shard(cwlb_shard* sh, const int32_t* d_rowoff_local, const int32_t* d
         return;
     }
     launch_sort_by_degree(ctx, sh->n, sh->nnz, d_rowoff_local, d_col, d_val, org, sro, scol, sval);
+    if (sh->nnz > 0) {
+        DeviceBuffer flag;
+        sh->unit = values_all_one(ctx, sval, nnz,
+                                  static_cast<unsigned int*>(flag.ensure(sizeof(unsigned int))));
+    }
     const int64_t cnt = run_partition(ctx, sh->n, sro, costs, capacity);
     sh->segment = cwlb_segment_size(&costs, capacity);
     sh->n_tasks = cnt;
@@ -204,7 +210,8 @@ void shard_aggregate(cwlb_shard* sh, const float* d_H, int64_t h_rows, int64_t K
     CWLB_CUDA(cudaSetDevice(sh->ctx->device));
     if (sh->n == 0 || K == 0) return;
     launch_spmm_mean(sh->ctx, sh->n, sh->nnz, sh->rowoff.as<int32_t>(0), sh->col.as<int32_t>(0),
-                     sh->val.as<float>(0), sh->origin.as<int32_t>(0), d_H, h_rows, K,
+                     sh->unit ? nullptr : sh->val.as<float>(0), sh->origin.as<int32_t>(0), d_H,
+                     h_rows, K,
                      sh->tasks.as<cwlb_task>(0), sh->n_tasks, d_out, sh->flags | flags);
 }
 

@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(kPlanThreads)
     merge_start(rowoff, n_rows, nnz, col, tasks, gtask, g, R, lane, m);
     uint32_t bad = 0;
     if (m.pos < m.end) {
-        if (val[m.pos] != 1.0f) bad |= kBadValue;
+        if (val && val[m.pos] != 1.0f) bad |= kBadValue;
         // A stored column equal to the end marker (never a valid index of H)
         // would end this member early: refuse to group instead.
         if (m.cur == kEnd || (m.pos + 1 < m.end && m.nxt == kEnd)) bad |= kUnsorted;
@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(kPlanThreads)
         ++k;
         if (m.pos != prev_pos && m.pos < m.end) {
             if (m.cur < prev_cur) bad |= kUnsorted;
-            if (val[m.pos] != 1.0f) bad |= kBadValue;
+            if (val && val[m.pos] != 1.0f) bad |= kBadValue;
             if (m.pos + 1 < m.end && m.nxt == kEnd) bad |= kUnsorted;
         }
     }
@@ -750,6 +750,14 @@ cwlb_plan* plan_create(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t
     p->n_tasks = n_tasks;
     p->n_rest = n_tasks;
     try {
+        // Values that are all 1.0 are not read at all (the task kernel's
+        // unit-value instances); the plan then keeps no value pointer.
+        if (nnz > 0) {
+            DeviceBuffer flag;
+            if (values_all_one(ctx, val, static_cast<size_t>(nnz),
+                               static_cast<unsigned int*>(flag.ensure(sizeof(unsigned int)))))
+                p->val = nullptr;
+        }
         if (group_size == 0) group_size = 4;  // measured faster than 8 on B200
         if (group_size <= 1) {
             p->off_reason |= CWLB_PLAN_DISABLED;

@@ -193,7 +193,7 @@ struct VecCfg {
 // <16,1>, <16,2> and <32,1> shapes outside short-row mode; short-row mode was
 // 10% slower with it (configuration 4), and wider or narrower shapes gain
 // registers and lose an occupancy step.
-template <int L, int V, bool kPrefetch>
+template <int L, int V, bool kPrefetch, bool kUnit>
 __device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, int32_t end,
                                               int32_t step, unsigned gmask, int lg,
                                               const float4* const (&hq)[V], const bool (&ok)[V],
@@ -204,13 +204,14 @@ __device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, 
     if constexpr (kPrefetch) {
         if (start < end && lg < min(L, end - start)) {
             nc = __ldg(a.col + start + lg);
-            nv = __ldg(a.val + start + lg);
+            nv = kUnit ? 1.0f : __ldg(a.val + start + lg);
         }
     }
     for (int32_t pos = start; pos < end; pos += step) {
         const int32_t cnt = min(L, end - pos);
         int32_t c = 0;
         float v = 0.0f;
+        bool bad = false;
         if constexpr (kPrefetch) {
             if (lg < cnt) {
                 c = nc;
@@ -221,24 +222,29 @@ __device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, 
             nv = 0.0f;
             if (np < end && lg < min(L, end - np)) {
                 nc = __ldg(a.col + np + lg);
-                nv = __ldg(a.val + np + lg);
+                nv = kUnit ? 1.0f : __ldg(a.val + np + lg);
             }
             if (lg < cnt && static_cast<uint32_t>(c) >= static_cast<uint64_t>(a.h_rows)) {
                 raise_err(a.err, CWLB_DEVERR_COL_RANGE);
                 c = 0;
                 v = 0.0f;
+                bad = true;
             }
         } else {
             if (lg < cnt) {
                 c = __ldg(a.col + pos + lg);
-                v = __ldg(a.val + pos + lg);
+                v = kUnit ? 1.0f : __ldg(a.val + pos + lg);
                 if (static_cast<uint32_t>(c) >= static_cast<uint64_t>(a.h_rows)) {
                     raise_err(a.err, CWLB_DEVERR_COL_RANGE);
                     c = 0;
                     v = 0.0f;
+                    bad = true;
                 }
             }
         }
+        // Unit values skip the value broadcast, except in a chunk holding an
+        // out-of-range column, whose value 0 must reach the group.
+        [[maybe_unused]] const bool chunk_bad = kUnit && __any_sync(gmask, bad);
         if (cnt == L) {
 #pragma unroll
             for (int u0 = 0; u0 < L; u0 += U) {
@@ -247,7 +253,9 @@ __device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, 
 #pragma unroll
                 for (int t = 0; t < U; ++t) {
                     cu[t] = static_cast<uint32_t>(__shfl_sync(gmask, c, u0 + t, L));
-                    vu[t] = __shfl_sync(gmask, v, u0 + t, L);
+                    // Unit values (all 1.0) need no broadcast: fma(1, x, acc)
+                    // rounds exactly as acc + x.
+                    vu[t] = (kUnit && !chunk_bad) ? 1.0f : __shfl_sync(gmask, v, u0 + t, L);
                 }
                 float4 x[U][V];
 #pragma unroll
@@ -270,7 +278,7 @@ __device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, 
                 for (int t = 0; t < U; ++t) {
                     const int src = (u0 + t) & (L - 1);
                     cu[t] = static_cast<uint32_t>(__shfl_sync(gmask, c, src, L));
-                    vu[t] = __shfl_sync(gmask, v, src, L);
+                    vu[t] = (kUnit && !chunk_bad) ? 1.0f : __shfl_sync(gmask, v, src, L);
                 }
                 float4 x[U][V];
 #pragma unroll
@@ -338,7 +346,7 @@ __device__ __forceinline__ void write_zero_row(const SpmmArgs& a, int32_t orig,
 // Rows of a task staged per warp in short-row mode (see launch_spmm_mean).
 constexpr int kStageRows = 128;
 
-template <int L, int V, bool kStage>
+template <int L, int V, bool kStage, bool kUnit>
 __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
     constexpr int G = VecCfg<L, V>::G;
     const int lane = threadIdx.x & 31;
@@ -424,7 +432,7 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
             float4 acc[V];
 #pragma unroll
             for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            gather_chunks<L, V, !kStage && L >= 16 && L * V <= 32>(a, f.base + f.begin + gt * L, f.base + f.end, team_lanes, gmask, lg,
+            gather_chunks<L, V, !kStage && L >= 16 && L * V <= 32, kUnit>(a, f.base + f.begin + gt * L, f.base + f.end, team_lanes, gmask, lg,
                                 hq, ok, K4, acc);
             for (int sh = L; sh < team_lanes; sh <<= 1) {
 #pragma unroll
@@ -450,7 +458,7 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
         float4 acc[V];
 #pragma unroll
         for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        gather_chunks<L, V, !kStage && L >= 16 && L * V <= 32>(a, f.base + f.begin + g * L, f.base + f.end, 32, gmask, lg, hq, ok,
+        gather_chunks<L, V, !kStage && L >= 16 && L * V <= 32, kUnit>(a, f.base + f.begin + g * L, f.base + f.end, 32, gmask, lg, hq, ok,
                             K4, acc);
 #pragma unroll
         for (int s = L; s < 32; s <<= 1) {
@@ -503,7 +511,7 @@ __global__ void __launch_bounds__(kThreads) spmm_scalar_kernel(SpmmArgs a) {
         for (int i = 0; i < V; ++i) acc[i] = 0.0f;
         for (int32_t j = f.base + f.begin; j < f.base + f.end; ++j) {
             int32_t c = __ldg(a.col + j);
-            float v = __ldg(a.val + j);
+            float v = a.val ? __ldg(a.val + j) : 1.0f;
             if (static_cast<uint64_t>(c) >= static_cast<uint64_t>(a.h_rows)) {
                 raise_err(a.err, CWLB_DEVERR_COL_RANGE);
                 c = 0;
@@ -738,10 +746,14 @@ void launch_vec(const SpmmArgs& a, bool stage, cudaStream_t s) {
     const int64_t tiles = ceil_div(K4, L * V);
     dim3 grid(static_cast<unsigned>(ceil_div(a.n_slots, kWarpsPerCta)),
               static_cast<unsigned>(tiles));
+    // Values NULL: every value is 1.0 (the instances without value loads).
+    const bool unit = a.val == nullptr;
     if (stage) {
-        spmm_vec_kernel<L, V, true><<<grid, kThreads, 0, s>>>(a);
+        if (unit) spmm_vec_kernel<L, V, true, true><<<grid, kThreads, 0, s>>>(a);
+        else spmm_vec_kernel<L, V, true, false><<<grid, kThreads, 0, s>>>(a);
     } else {
-        spmm_vec_kernel<L, V, false><<<grid, kThreads, 0, s>>>(a);
+        if (unit) spmm_vec_kernel<L, V, false, true><<<grid, kThreads, 0, s>>>(a);
+        else spmm_vec_kernel<L, V, false, false><<<grid, kThreads, 0, s>>>(a);
     }
 }
 
@@ -963,21 +975,31 @@ spmm_mean_reference_kernel(const int32_t* __restrict__ rowoff, const int32_t* __
 }  // namespace
 
 namespace {
-__global__ void fill_ones_kernel(float* __restrict__ dst, size_t count) {
+// Sets *other when some value is not exactly 1.0f (compared as bits, so
+// -0.0 and NaN payloads count as other values).
+__global__ void values_other_kernel(const float* __restrict__ v, size_t count,
+                                    unsigned int* __restrict__ other) {
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    unsigned int acc = 0;
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
          i += stride)
-        dst[i] = 1.0f;
+        acc |= __float_as_uint(v[i]) ^ 0x3f800000u;
+    if (__any_sync(0xffffffffu, acc != 0) && (threadIdx.x & 31) == 0) atomicOr(other, 1u);
 }
 }  // namespace
 
-void launch_fill_ones(cwlb_ctx* ctx, float* dst, size_t count) {
-    if (count == 0) return;
+bool values_all_one(cwlb_ctx* ctx, const float* d_val, size_t count, unsigned int* d_flag) {
+    if (count == 0) return true;
+    CWLB_CUDA(cudaMemsetAsync(d_flag, 0, sizeof(unsigned int), ctx->stream));
     const unsigned blocks = static_cast<unsigned>(
         std::min<int64_t>(ceil_div(static_cast<int64_t>(count), kThreads),
                           static_cast<int64_t>(ctx->props.multiProcessorCount) * 8));
-    fill_ones_kernel<<<blocks, kThreads, 0, ctx->stream>>>(dst, count);
-    CWLB_LAUNCH_CHECK("fill_ones_kernel");
+    values_other_kernel<<<blocks, kThreads, 0, ctx->stream>>>(d_val, count, d_flag);
+    CWLB_LAUNCH_CHECK("values_other_kernel");
+    unsigned int h = 0;
+    CWLB_CUDA(cudaMemcpyAsync(&h, d_flag, sizeof(h), cudaMemcpyDeviceToHost, ctx->stream));
+    CWLB_CUDA(cudaStreamSynchronize(ctx->stream));
+    return h == 0;
 }
 
 void launch_spmm_mean_reference(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
