@@ -211,7 +211,6 @@ __device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, 
         const int32_t cnt = min(L, end - pos);
         int32_t c = 0;
         float v = 0.0f;
-        bool bad = false;
         if constexpr (kPrefetch) {
             if (lg < cnt) {
                 c = nc;
@@ -228,7 +227,6 @@ __device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, 
                 raise_err(a.err, CWLB_DEVERR_COL_RANGE);
                 c = 0;
                 v = 0.0f;
-                bad = true;
             }
         } else {
             if (lg < cnt) {
@@ -238,13 +236,10 @@ __device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, 
                     raise_err(a.err, CWLB_DEVERR_COL_RANGE);
                     c = 0;
                     v = 0.0f;
-                    bad = true;
                 }
             }
         }
-        // Unit values skip the value broadcast, except in a chunk holding an
-        // out-of-range column, whose value 0 must reach the group.
-        [[maybe_unused]] const bool chunk_bad = kUnit && __any_sync(gmask, bad);
+
         if (cnt == L) {
 #pragma unroll
             for (int u0 = 0; u0 < L; u0 += U) {
@@ -254,8 +249,9 @@ __device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, 
                 for (int t = 0; t < U; ++t) {
                     cu[t] = static_cast<uint32_t>(__shfl_sync(gmask, c, u0 + t, L));
                     // Unit values (all 1.0) need no broadcast: fma(1, x, acc)
-                    // rounds exactly as acc + x.
-                    vu[t] = (kUnit && !chunk_bad) ? 1.0f : __shfl_sync(gmask, v, u0 + t, L);
+                    // rounds exactly as acc + x.  (An out-of-range column is
+                    // still flagged; its row 0 is then added, not skipped.)
+                    vu[t] = kUnit ? 1.0f : __shfl_sync(gmask, v, u0 + t, L);
                 }
                 float4 x[U][V];
 #pragma unroll
@@ -278,7 +274,7 @@ __device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, 
                 for (int t = 0; t < U; ++t) {
                     const int src = (u0 + t) & (L - 1);
                     cu[t] = static_cast<uint32_t>(__shfl_sync(gmask, c, src, L));
-                    vu[t] = (kUnit && !chunk_bad) ? 1.0f : __shfl_sync(gmask, v, src, L);
+                    vu[t] = kUnit ? 1.0f : __shfl_sync(gmask, v, src, L);
                 }
                 float4 x[U][V];
 #pragma unroll
@@ -746,14 +742,16 @@ void launch_vec(const SpmmArgs& a, bool stage, cudaStream_t s) {
     const int64_t tiles = ceil_div(K4, L * V);
     dim3 grid(static_cast<unsigned>(ceil_div(a.n_slots, kWarpsPerCta)),
               static_cast<unsigned>(tiles));
-    // Values NULL: every value is 1.0 (the instances without value loads).
-    const bool unit = a.val == nullptr;
+    // Values NULL (every value 1.0): the instances without value loads and
+    // broadcasts (12% on configuration 5).  The short-row instance was 4%
+    // slower that way (configuration 4); launch_spmm_mean gives it an array
+    // of ones instead, so it never sees NULL.
     if (stage) {
-        if (unit) spmm_vec_kernel<L, V, true, true><<<grid, kThreads, 0, s>>>(a);
-        else spmm_vec_kernel<L, V, true, false><<<grid, kThreads, 0, s>>>(a);
+        spmm_vec_kernel<L, V, true, false><<<grid, kThreads, 0, s>>>(a);
+    } else if (a.val == nullptr) {
+        spmm_vec_kernel<L, V, false, true><<<grid, kThreads, 0, s>>>(a);
     } else {
-        if (unit) spmm_vec_kernel<L, V, false, true><<<grid, kThreads, 0, s>>>(a);
-        else spmm_vec_kernel<L, V, false, false><<<grid, kThreads, 0, s>>>(a);
+        spmm_vec_kernel<L, V, false, false><<<grid, kThreads, 0, s>>>(a);
     }
 }
 
@@ -886,6 +884,7 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
         // It costs 8 KB of shared memory per CTA, taken from L1, so
         // hub-heavy graphs with few rows per task keep the plain kernel.
         const bool stage = static_cast<int64_t>(n_rows) >= 16 * n_tasks;
+        if (stage && a.val == nullptr && nnz > 0) a.val = ones_array(ctx, nnz);
         switch (L) {
             case 1: launch_vec_v<1>(V, a, stage, s); break;
             case 2: launch_vec_v<2>(V, a, stage, s); break;
@@ -975,6 +974,13 @@ spmm_mean_reference_kernel(const int32_t* __restrict__ rowoff, const int32_t* __
 }  // namespace
 
 namespace {
+__global__ void fill_ones_kernel(float* __restrict__ dst, size_t count) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+         i += stride)
+        dst[i] = 1.0f;
+}
+
 // Sets *other when some value is not exactly 1.0f (compared as bits, so
 // -0.0 and NaN payloads count as other values).
 __global__ void values_other_kernel(const float* __restrict__ v, size_t count,
@@ -987,6 +993,20 @@ __global__ void values_other_kernel(const float* __restrict__ v, size_t count,
     if (__any_sync(0xffffffffu, acc != 0) && (threadIdx.x & 31) == 0) atomicOr(other, 1u);
 }
 }  // namespace
+
+const float* ones_array(cwlb_ctx* ctx, int32_t count) {
+    const size_t n = static_cast<size_t>(count);
+    if (ctx->ones_count < n) {
+        float* d = ctx->ones.as<float>(n);
+        const unsigned blocks = static_cast<unsigned>(
+            std::min<int64_t>(ceil_div(static_cast<int64_t>(n), kThreads),
+                              static_cast<int64_t>(ctx->props.multiProcessorCount) * 8));
+        fill_ones_kernel<<<blocks, kThreads, 0, ctx->stream>>>(d, n);
+        CWLB_LAUNCH_CHECK("fill_ones_kernel");
+        ctx->ones_count = n;
+    }
+    return static_cast<const float*>(ctx->ones.ptr);
+}
 
 bool values_all_one(cwlb_ctx* ctx, const float* d_val, size_t count, unsigned int* d_flag) {
     if (count == 0) return true;

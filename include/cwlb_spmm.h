@@ -137,8 +137,11 @@ int cwlb_spmm_kernel_large_k(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
  * (see cwlb_tasks_check); the kernels then write every output row themselves
  * and the full zero-fill is skipped.
  * d_value may be NULL: every value is then 1.0 (the reference's text loader
- * gives every stored entry the value 1, src/data.cpp:115) and no value is
- * read; the result is bit-identical to passing an array of ones.
+ * gives every stored entry the value 1, src/data.cpp:115) and the kernels
+ * need not read values; the result equals passing an array of ones (bit for
+ * bit where the merge order is fixed).  On invalid input the two differ: an
+ * out-of-range column raises CWLB_DEVERR_COL_RANGE either way, but with NULL
+ * values its row is not skipped (the output is then undefined).
  * CWLB_DETERMINISTIC -> rows split across tasks are merged in a fixed order
  * (fragment partials kept in context scratch of up to 2 x n_tasks x K floats,
  * then summed per row in task order, in blocks of 64 fragments) instead of
