@@ -38,7 +38,7 @@ def ctx():
     c.close()
 
 
-def _sorted_graph(oracle, scale=14, edges=400_000, seed=51, values=None, shuffle_rows=False):
+def _sorted_graph(oracle, scale=13, edges=600_000, seed=51, values=None, shuffle_rows=False):
     ro, col, val = graphs.rmat_np(scale, edges, 0.57, 0.19, 0.19, seed=seed, symmetrize=True,
                                   drop_self_loops=True, dedupe=True)
     if values is not None:
