@@ -175,7 +175,9 @@ __device__ __forceinline__ bool load_task(const SpmmArgs& a, int64_t t, cwlb_tas
 template <int L, int V>
 struct VecCfg {
     static constexpr int G = 32 / L;
-    static constexpr int U0 = V == 1 ? 8 : (V == 2 ? 4 : 2);
+    // Nonzeros gathered per step: 4 for one or two float4 per lane (with one
+    // float4, 8 in flight cost configuration 5 4% against 4), 2 for wider.
+    static constexpr int U0 = V <= 2 ? 4 : 2;
     static constexpr int U = U0 < L ? U0 : L;
     // Rows of at most 64 floats (short-row graphs): partial chunks skip the
     // X loads of their unused slots.  Wider shapes load unconditionally: the
