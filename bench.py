@@ -76,6 +76,10 @@ def parse_args():
                     help="N = 1: time an aggregation plan (cwlb_plan_*, built outside the timed "
                          "region) with this group size (0 = the library's choice) instead of "
                          "the task kernel")
+    ap.add_argument("--rebalance", type=int, default=2, metavar="ROUNDS",
+                    help="N > 1: re-cut the shards up to ROUNDS times by their measured "
+                         "aggregation times (cwlb_shard_bounds_rebalance), before the timed "
+                         "region; 0 keeps the cost-model cut")
     ap.add_argument("--x-sharded", action="store_true",
                     help="N > 1: X arrives row-sharded (as a prior layer leaves it); every "
                          "step all-gathers it over NCCL before the aggregation")
@@ -191,8 +195,21 @@ def dist_setup(args):
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+        # NCCL prints its version line on standard output when it creates the
+        # communicator (eagerly here, with device_id); send it to standard
+        # error so that the bench line stays the only line on standard output.
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local))
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     return world, rank, local
 
 
@@ -228,25 +245,29 @@ def barrier(world):
 # workload
 
 def build_workload(cfg_id, device, world, rank, costs, scale_down=1):
-    import torch
     rowoff, col, val, X = graphs.build_config_torch(cfg_id, device, scale_down=scale_down)
-    a, b = shards.shard_bounds(rowoff, costs.C_compute_ns + costs.C_load_ns, costs.C_store_ns,
-                               world, rank)
-    bounds = [shards.shard_bounds(rowoff, costs.C_compute_ns + costs.C_load_ns,
-                                  costs.C_store_ns, world, r) for r in range(world)]
-    e0, e1 = int(rowoff[a]), int(rowoff[b])
-    ro = (rowoff[a:b + 1] - e0).contiguous()
-    sub_col = col[e0:e1].contiguous()
-    sub_val = val[e0:e1].contiguous()
-    wl = dict(rowoff=ro, col=sub_col, val=sub_val, X=X, n=b - a, nnz=e1 - e0, row0=a,
-              bounds=bounds,
-              nnz_total=int(rowoff[-1]), n_total=rowoff.numel() - 1, K=X.shape[1],
-              distinct_cols=int(torch.unique(sub_col).numel()) if e1 > e0 else 0)
-    if world > 1:
-        # The whole graph stays on every rank's GPU: the library's shard
-        # entry point (cwlb_shard_create_device) cuts and sorts its block.
-        wl["full"] = (rowoff, col, val)
+    cut = [0] + [shards.shard_bounds(rowoff, costs.C_compute_ns + costs.C_load_ns,
+                                     costs.C_store_ns, world, r)[1] for r in range(world)]
+    # The whole graph stays on every rank's GPU: with N > 1 the library's
+    # shard entry point (cwlb_shard_create_device) cuts and sorts its block.
+    wl = dict(full=(rowoff, col, val), X=X, world=world, nnz_total=int(rowoff[-1]),
+              n_total=rowoff.numel() - 1, K=X.shape[1])
+    set_block(wl, cut, rank)
     return wl
+
+
+def set_block(wl, cut, rank):
+    """This rank's block of ORIGINAL rows [cut[rank], cut[rank + 1])."""
+    import torch
+    rowoff, col, val = wl["full"]
+    a, b = int(cut[rank]), int(cut[rank + 1])
+    e0, e1 = int(rowoff[a]), int(rowoff[b])
+    sub_col = col[e0:e1].contiguous()
+    wl.update(rowoff=(rowoff[a:b + 1] - e0).contiguous(), col=sub_col,
+              val=val[e0:e1].contiguous(), n=b - a, nnz=e1 - e0, row0=a,
+              cut=np.asarray(cut, np.int32),
+              bounds=[(int(cut[r]), int(cut[r + 1])) for r in range(wl["world"])],
+              distinct_cols=int(torch.unique(sub_col).numel()) if e1 > e0 else 0)
 
 
 def device_prepare(ctx, wl):
@@ -319,14 +340,55 @@ def launches_per_step(flags, n_tasks, plan_groups=False):
 
 def make_shard(ctx, wl, costs, S, rank, world):
     """N > 1: this rank's shard through the library's multi-GPU entry point
-    (cut by cwlb_shard_bounds, sorted, partitioned and checked on this GPU)."""
+    (cut at wl["cut"], sorted, partitioned and checked on this GPU)."""
     import cwlb_spmm as cs
     ro, col, val = wl["full"]
     sh = cs.Shard.from_device(ctx, wl["n_total"], wl["nnz_total"], ro.data_ptr(), col.data_ptr(),
-                              val.data_ptr(), costs, cs.capacity_from_s(S, costs), rank, world)
+                              val.data_ptr(), costs, cs.capacity_from_s(S, costs), rank, world,
+                              cut=wl["cut"])
     assert (sh.row_begin, sh.row_end) == tuple(wl["bounds"][rank]), "shard cut differs"
     assert sh.nnz == wl["nnz"]
     return sh
+
+
+def rebalance_shards(ctx, wl, costs, S, rank, world, rounds):
+    """N > 1: re-cut the shards by their measured aggregation times
+    (cwlb_shard_bounds_rebalance), outside the timed region.  Every rank times
+    its own shard (3 warm-up + 10 timed aggregations); the times are
+    all-gathered, so every rank computes the same cut.  Returns the history."""
+    import torch
+    import cwlb_spmm as cs
+    ro_h = wl["full"][0].cpu().numpy()
+    history = []
+    for _ in range(rounds + 1):
+        if wl.get("shard") is not None:
+            wl["shard"].close()
+        wl["shard"] = make_shard(ctx, wl, costs, S, rank, world)
+        out = torch.empty((max(wl["n"], 1), wl["K"]), dtype=torch.float32, device=wl["X"].device)
+        for _ in range(3):
+            run_step(ctx, wl, None, 0, out, 0)
+        t = time_steps(ctx, wl, None, 0, out, 0, 10) / 10
+        times = allgather_values(t, world)
+        history.append({"cut": wl["cut"].tolist(),
+                        "ms_by_rank": [round(v * 1e3, 4) for v in times]})
+        if len(history) > rounds:
+            break
+        new = cs.shard_bounds_rebalance(ro_h, costs, wl["cut"], times)
+        if np.array_equal(new, wl["cut"]):
+            break
+        set_block(wl, new, rank)
+        device_prepare(ctx, wl)
+    # Keep the best cut seen (timing noise can make a late round worse).
+    best = min(range(len(history)), key=lambda i: max(history[i]["ms_by_rank"]))
+    if history[best]["cut"] != wl["cut"].tolist():
+        set_block(wl, history[best]["cut"], rank)
+        device_prepare(ctx, wl)
+    if wl.get("shard") is not None:
+        wl["shard"].close()
+        wl["shard"] = None
+    return {"rule": "cwlb_shard_bounds, then cwlb_shard_bounds_rebalance by the measured "
+                    "shard times (one aggregation each, all-gathered)",
+            "rounds": history, "kept": best, "cut": wl["cut"].tolist()}
 
 
 def run_step(ctx, wl, tasks, n_tasks, out, flags):
@@ -538,13 +600,6 @@ def run_ours(args):
     device_prepare(ctx, wl)
     K = wl["K"]
     x_full = wl["X"]
-    if args.x_sharded and world > 1:
-        # X as a prior layer leaves it: this rank holds only its own rows; the
-        # rest is poisoned so that only the per-step all-gather can fill it.
-        a, b = wl["bounds"][rank]
-        xs = torch.full_like(x_full, float("nan"))
-        xs[a:b] = x_full[a:b]
-        wl.update(X=xs, x_sharded=True)
     out = torch.empty((max(wl["n"], 1), K), dtype=torch.float32, device=device)
 
     # S: the reference's --candidates procedure (main.cpp:534-577): three
@@ -574,6 +629,19 @@ def run_ours(args):
         if best is None or t < best[0]:
             best = (t, S)
     S = best[1]
+    cut_info = None
+    if world > 1:
+        cut_info = {"rule": "cwlb_shard_bounds", "cut": wl["cut"].tolist()}
+        if args.rebalance > 0:
+            cut_info = rebalance_shards(ctx, wl, costs, S, rank, world, args.rebalance)
+            out = torch.empty((max(wl["n"], 1), K), dtype=torch.float32, device=device)
+    if args.x_sharded and world > 1:
+        # X as a prior layer leaves it: this rank holds only its own rows; the
+        # rest is poisoned so that only the per-step all-gather can fill it.
+        a, b = wl["bounds"][rank]
+        xs = torch.full_like(x_full, float("nan"))
+        xs[a:b] = x_full[a:b]
+        wl.update(X=xs, x_sharded=True)
     # Partition latency as a caller sees it (the call synchronises to size
     # its output): device partitioner for the chosen S.
     torch.cuda.synchronize()
@@ -732,6 +800,7 @@ def run_ours(args):
                        "n_tasks_rank0": n_tasks, "costs": os.path.relpath(COSTS_FILE, ROOT),
                        "parallelism": f"row shards x{world}" if world > 1 else "single GPU",
                        "process_group_world_size": pg_world,
+                       "shard_cut": cut_info,
                        "ms_per_step_by_rank": per_rank_ms,
                        "split_row_merge": "deterministic" if args.deterministic else "atomic",
                        "values": ("all 1.0, passed as NULL (no value loads)"

@@ -67,13 +67,21 @@ void need(bool ok, int code, const std::string& msg) {
 // Cut points of the cost-balanced row shards.  The arithmetic is sequential
 // float64, multiply and add rounded separately (this file's host code is
 // built with -ffp-contract=off), so the cuts are reproducible bit for bit.
+// With old_bounds / scale, the weight of every row of old shard g is
+// multiplied by scale[g] (the rebalancing cut).
 void shard_bounds_host(int32_t n_rows, const int32_t* rowoff, double edge_w, double store_w,
-                       int32_t n_shards, int32_t* bounds) {
+                       int32_t n_shards, int32_t* bounds, const int32_t* old_bounds = nullptr,
+                       const double* scale = nullptr) {
     std::vector<double> cum(static_cast<size_t>(n_rows));
     double acc = 0.0;
+    int32_t g = 0;
     for (int32_t r = 0; r < n_rows; ++r) {
         const double deg = static_cast<double>(static_cast<int64_t>(rowoff[r + 1]) - rowoff[r]);
-        const double w = deg * edge_w + store_w;
+        double w = deg * edge_w + store_w;
+        if (scale) {
+            while (r >= old_bounds[g + 1]) ++g;
+            w = w * scale[g];
+        }
         acc = acc + w;
         cum[static_cast<size_t>(r)] = acc;
     }
@@ -89,6 +97,27 @@ void shard_bounds_host(int32_t n_rows, const int32_t* rowoff, double edge_w, dou
     }
     bounds[n_shards] = n_rows;
     for (int32_t k = 1; k <= n_shards; ++k) bounds[k] = std::max(bounds[k], bounds[k - 1]);
+}
+
+// Per-shard scale of the rebalancing cut: measured time / modelled weight
+// (1 for a shard without weight).
+std::vector<double> shard_scales(const int32_t* rowoff, double edge_w, double store_w,
+                                 int32_t n_shards, const int32_t* old_bounds,
+                                 const double* shard_time) {
+    std::vector<double> scale(static_cast<size_t>(n_shards), 1.0);
+    for (int32_t g = 0; g < n_shards; ++g) {
+        double W = 0.0;
+        for (int32_t r = old_bounds[g]; r < old_bounds[g + 1]; ++r) {
+            const double deg = static_cast<double>(static_cast<int64_t>(rowoff[r + 1]) - rowoff[r]);
+            W = W + (deg * edge_w + store_w);
+        }
+        if (W > 0.0) {
+            need(shard_time[g] > 0.0 && std::isfinite(shard_time[g]), CWLB_ERR_INVALID_ARGUMENT,
+                 "shard times must be positive and finite");
+            scale[static_cast<size_t>(g)] = shard_time[g] / W;
+        }
+    }
+    return scale;
 }
 
 __global__ void rebase_offsets_kernel(const int32_t* __restrict__ in, int64_t count, int32_t base,
@@ -263,6 +292,34 @@ int cwlb_shard_bounds(int32_t n_rows, const int32_t* row_offset, const cwlb_cost
     });
 }
 
+int cwlb_shard_bounds_rebalance(int32_t n_rows, const int32_t* row_offset,
+                                const cwlb_costs* costs, int32_t n_shards,
+                                const int32_t* bounds, const double* shard_time,
+                                int32_t* new_bounds) {
+    return cwlb::guarded_multi([&] {
+        cwlb::need(costs && bounds && shard_time && new_bounds && (n_rows == 0 || row_offset),
+                   CWLB_ERR_INVALID_ARGUMENT, "null argument");
+        cwlb::need(n_rows >= 0 && n_shards >= 1, CWLB_ERR_INVALID_ARGUMENT,
+                   "n_rows must be >= 0 and n_shards >= 1");
+        cwlb::need(bounds[0] == 0 && bounds[n_shards] == n_rows, CWLB_ERR_INVALID_ARGUMENT,
+                   "bounds must start at 0 and end at n_rows");
+        for (int32_t g = 0; g < n_shards; ++g)
+            cwlb::need(bounds[g] <= bounds[g + 1], CWLB_ERR_INVALID_ARGUMENT,
+                       "bounds must be non-decreasing");
+        if (n_rows == 0) {
+            std::fill(new_bounds, new_bounds + n_shards + 1, 0);
+            return;
+        }
+        const double ew = costs->C_compute_ns + costs->C_load_ns, sw = costs->C_store_ns;
+        const std::vector<double> scale =
+            cwlb::shard_scales(row_offset, ew, sw, n_shards, bounds, shard_time);
+        std::vector<int32_t> nb(static_cast<size_t>(n_shards) + 1);  // bounds may alias
+        cwlb::shard_bounds_host(n_rows, row_offset, ew, sw, n_shards, nb.data(), bounds,
+                                scale.data());
+        std::copy(nb.begin(), nb.end(), new_bounds);
+    });
+}
+
 int cwlb_shard_create(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* row_offset,
                       const int32_t* col_ind, const float* value, const cwlb_costs* costs,
                       double capacity, int32_t shard, int32_t n_shards, cwlb_shard** out) {
@@ -280,6 +337,15 @@ int cwlb_shard_create_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
                              const int32_t* d_row_offset, const int32_t* d_col_ind,
                              const float* d_value, const cwlb_costs* costs, double capacity,
                              int32_t shard, int32_t n_shards, cwlb_shard** out) {
+    return cwlb_shard_create_device_cut(ctx, n_rows, nnz, d_row_offset, d_col_ind, d_value, costs,
+                                        capacity, nullptr, shard, n_shards, out);
+}
+
+int cwlb_shard_create_device_cut(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
+                                 const int32_t* d_row_offset, const int32_t* d_col_ind,
+                                 const float* d_value, const cwlb_costs* costs, double capacity,
+                                 const int32_t* cut, int32_t shard, int32_t n_shards,
+                                 cwlb_shard** out) {
     return cwlb::guarded_multi([&] {
         cwlb::check_shard_args(ctx, n_rows, nnz, costs, shard, n_shards, out);
         *out = nullptr;
@@ -293,8 +359,17 @@ int cwlb_shard_create_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
         CWLB_CUDA(cudaStreamSynchronize(ctx->stream));
         cwlb::validate_offsets(n_rows, nnz, h.data());
         std::vector<int32_t> bounds(static_cast<size_t>(n_shards) + 1);
-        cwlb::shard_bounds_host(n_rows, h.data(), costs->C_compute_ns + costs->C_load_ns,
-                                costs->C_store_ns, n_shards, bounds.data());
+        if (cut) {
+            cwlb::need(cut[0] == 0 && cut[n_shards] == n_rows, CWLB_ERR_INVALID_ARGUMENT,
+                       "cut must start at 0 and end at n_rows");
+            for (int32_t g = 0; g < n_shards; ++g)
+                cwlb::need(cut[g] <= cut[g + 1], CWLB_ERR_INVALID_ARGUMENT,
+                           "cut must be non-decreasing");
+            std::copy(cut, cut + n_shards + 1, bounds.begin());
+        } else {
+            cwlb::shard_bounds_host(n_rows, h.data(), costs->C_compute_ns + costs->C_load_ns,
+                                    costs->C_store_ns, n_shards, bounds.data());
+        }
         cwlb_shard* sh = cwlb::new_shard(ctx, shard, n_shards, bounds.data(), h.data());
         try {
             const int32_t e0 = h[static_cast<size_t>(sh->row_begin)];

@@ -118,6 +118,9 @@ _sig("cwlb_shard_create", [_vp, _i32, _i32, _vp, _vp, _vp, C.POINTER(cwlb_costs)
                            _i32, C.POINTER(_vp)])
 _sig("cwlb_shard_create_device", [_vp, _i32, _i32, _vp, _vp, _vp, C.POINTER(cwlb_costs), _dbl,
                                   _i32, _i32, C.POINTER(_vp)])
+_sig("cwlb_shard_bounds_rebalance", [_i32, _vp, C.POINTER(cwlb_costs), _i32, _vp, _vp, _vp])
+_sig("cwlb_shard_create_device_cut", [_vp, _i32, _i32, _vp, _vp, _vp, C.POINTER(cwlb_costs),
+                                      _dbl, _vp, _i32, _i32, C.POINTER(_vp)])
 _sig("cwlb_shard_info", [_vp, C.POINTER(_i32), C.POINTER(_i32), C.POINTER(_i32), C.POINTER(_i64),
                          C.POINTER(_i32)])
 _sig("cwlb_shard_tasks", [_vp, C.POINTER(_vp)])
@@ -446,6 +449,23 @@ def shard_bounds(row_offset, costs: SpmmCostParams, n_shards: int) -> np.ndarray
     return b
 
 
+def shard_bounds_rebalance(row_offset, costs: SpmmCostParams, bounds, shard_time) -> np.ndarray:
+    """The cut of shard_bounds re-weighted by measured shard times: every row
+    of shard g under `bounds` weighs its whole-row weight times
+    shard_time[g] / (the shard's summed weight).  Host code."""
+    ro = np.ascontiguousarray(row_offset, np.int32)
+    n = max(len(ro) - 1, 0)
+    b = np.ascontiguousarray(bounds, np.int32)
+    t = np.ascontiguousarray(shard_time, np.float64)
+    G = len(b) - 1
+    if G < 1 or len(t) != G:
+        raise ValueError("need n_shards + 1 bounds and n_shards times")
+    nb = np.zeros(G + 1, np.int32)
+    c = costs.c()
+    _check(_lib.cwlb_shard_bounds_rebalance(n, _p(ro), C.byref(c), G, _p(b), _p(t), _p(nb)))
+    return nb
+
+
 class Shard:
     """One GPU's resident share of a multi-GPU aggregation: original rows
     [row_begin, row_end) sorted by degree and partitioned on that GPU."""
@@ -471,12 +491,23 @@ class Shard:
 
     @classmethod
     def from_device(cls, ctx: "Context", n_rows, nnz, d_rowoff, d_col, d_val,
-                    costs: SpmmCostParams, capacity: float, shard: int, n_shards: int) -> "Shard":
+                    costs: SpmmCostParams, capacity: float, shard: int, n_shards: int,
+                    cut=None) -> "Shard":
+        """cut: n_shards + 1 cut points (e.g. from shard_bounds_rebalance);
+        None cuts as shard_bounds."""
         h = _vp()
         c = costs.c()
-        _check(_lib.cwlb_shard_create_device(ctx.handle, n_rows, nnz, d_rowoff, d_col, d_val,
-                                             C.byref(c), float(capacity), shard, n_shards,
-                                             C.byref(h)))
+        if cut is None:
+            _check(_lib.cwlb_shard_create_device(ctx.handle, n_rows, nnz, d_rowoff, d_col, d_val,
+                                                 C.byref(c), float(capacity), shard, n_shards,
+                                                 C.byref(h)))
+        else:
+            cb = np.ascontiguousarray(cut, np.int32)
+            if len(cb) != n_shards + 1:
+                raise ValueError("cut needs n_shards + 1 entries")
+            _check(_lib.cwlb_shard_create_device_cut(ctx.handle, n_rows, nnz, d_rowoff, d_col,
+                                                     d_val, C.byref(c), float(capacity), _p(cb),
+                                                     shard, n_shards, C.byref(h)))
         return cls(ctx, h)
 
     @property

@@ -285,6 +285,23 @@ int cwlb_partition_device_noalloc(void* cuda_stream, int32_t n_rows, const int32
 int cwlb_shard_bounds(int32_t n_rows, const int32_t* row_offset, const cwlb_costs* costs,
                       int32_t n_shards, int32_t* bounds);
 
+/* The same rule re-weighted by measured shard times: every row of shard g
+ * under `bounds` (n_shards + 1 cut points, from 0 to n_rows, non-decreasing)
+ * weighs its whole-row weight times shard_time[g] / W_g, W_g being the shard's
+ * summed weight under that cut (shards without weight keep factor 1), and
+ * new_bounds receives the cut of the re-weighted prefix sum (same sequential
+ * float64 rule; new_bounds may alias bounds).  The kernel's real cost per row
+ * differs from the modelled one by degree class (on a B200, a row of a few
+ * nonzeros costs about as much as 17 nonzeros of a hub row at K = 64); the
+ * times of one aggregation of each shard fold that back into the cut.  Every
+ * GPU of a job must pass the same times (e.g. all-gathered) to get the same
+ * cut.  CWLB_ERR_INVALID_ARGUMENT for bad bounds, or a non-positive or
+ * non-finite time of a shard with weight.  Host code; no device needed. */
+int cwlb_shard_bounds_rebalance(int32_t n_rows, const int32_t* row_offset,
+                                const cwlb_costs* costs, int32_t n_shards,
+                                const int32_t* bounds, const double* shard_time,
+                                int32_t* new_bounds);
+
 typedef struct cwlb_shard cwlb_shard;
 
 /* Builds shard `shard` of `n_shards` on ctx's device from the caller's whole
@@ -303,6 +320,14 @@ int cwlb_shard_create_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
                              const int32_t* d_row_offset, const int32_t* d_col_ind,
                              const float* d_value, const cwlb_costs* costs, double capacity,
                              int32_t shard, int32_t n_shards, cwlb_shard** out);
+/* cwlb_shard_create_device with the cut given: `cut` holds n_shards + 1
+ * host ints from 0 to n_rows, non-decreasing (e.g. from
+ * cwlb_shard_bounds_rebalance); NULL cuts as cwlb_shard_bounds. */
+int cwlb_shard_create_device_cut(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
+                                 const int32_t* d_row_offset, const int32_t* d_col_ind,
+                                 const float* d_value, const cwlb_costs* costs, double capacity,
+                                 const int32_t* cut, int32_t shard, int32_t n_shards,
+                                 cwlb_shard** out);
 /* The shard's original rows [*row_begin, *row_end), its nonzeros, task count
  * and the segment size S the partitioner derived; NULL outputs are skipped. */
 int cwlb_shard_info(const cwlb_shard* shard, int32_t* row_begin, int32_t* row_end, int32_t* nnz,

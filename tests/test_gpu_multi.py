@@ -8,7 +8,8 @@ src/parallelMatrix.cpp:151-236 aggregation), so:
     run on the same block: its task list bit for bit;
   * the assembled output against the oracle's float64 mean of the whole
     graph, within the condition-relative 1e-5 of tests/helpers.py;
-  * the shard cuts equal cwlb_shard_bounds.
+  * the shard cuts equal cwlb_shard_bounds, or the cut given explicitly
+    (cwlb_shard_create_device_cut, e.g. a cwlb_shard_bounds_rebalance cut).
 Most tests run on one B200: two contexts on device 0 are two "GPUs" to the
 library (two host threads, two streams), which exercises the sharding, the
 threads and the output assembly; the two-GPU test skips on a one-GPU box.
@@ -69,12 +70,18 @@ def test_multi_entry_point_on_contexts_of_one_gpu(oracle, G, K):
             c.close()
 
 
-def test_shards_from_device_memory_match_the_oracle_block_by_block(oracle):
+@pytest.mark.parametrize("rebalanced", [False, True])
+def test_shards_from_device_memory_match_the_oracle_block_by_block(oracle, rebalanced):
     csr, X = _graph()
     G, S = 3, 40
     cap = cs.capacity_from_s(S, COSTS)
     costs_l = [COSTS.C_compute_ns, COSTS.C_load_ns, COSTS.C_store_ns, COSTS.C_atomic_ns]
     bounds = cs.shard_bounds(csr.RowOffset, COSTS, G)
+    cut = None
+    if rebalanced:  # a cut re-weighted by (made-up) shard times, given explicitly
+        cut = cs.shard_bounds_rebalance(csr.RowOffset, COSTS, bounds, [1.0, 2.5, 0.7])
+        assert not np.array_equal(cut, bounds)
+        bounds = cut
     with cs.Context(0) as ctx:
         ctx.set_stream(torch.cuda.current_stream().cuda_stream)
         d_ro = torch.from_numpy(csr.RowOffset).cuda()
@@ -84,7 +91,7 @@ def test_shards_from_device_memory_match_the_oracle_block_by_block(oracle):
         out = torch.full((csr.rows, X.shape[1]), float("nan"), device="cuda")
         for s in range(G):
             sh = cs.Shard.from_device(ctx, csr.rows, csr.nnz, d_ro.data_ptr(), d_col.data_ptr(),
-                                      d_val.data_ptr(), COSTS, cap, s, G)
+                                      d_val.data_ptr(), COSTS, cap, s, G, cut=cut)
             try:
                 assert (sh.row_begin, sh.row_end) == (bounds[s], bounds[s + 1])
                 a, b = sh.row_begin, sh.row_end
@@ -137,6 +144,13 @@ def test_multi_argument_errors():
             cs.spmm_mean_multi([c0], bad, X, COSTS, 10.0)
         with pytest.raises(ValueError, match="shard index"):
             cs.Shard.from_host(c0, csr, COSTS, 10.0, 2, 2)
+        d_ro = torch.from_numpy(csr.RowOffset).cuda()
+        d_col = torch.from_numpy(csr.ColInd).cuda()
+        d_val = torch.from_numpy(csr.Value).cuda()
+        for bad_cut in ([0, 5, 3], [1, 5, csr.rows], [0, 5, csr.rows - 1]):
+            with pytest.raises(ValueError, match="cut must"):
+                cs.Shard.from_device(c0, csr.rows, csr.nnz, d_ro.data_ptr(), d_col.data_ptr(),
+                                     d_val.data_ptr(), COSTS, 10.0, 0, 2, cut=bad_cut)
     finally:
         c0.close()
 
