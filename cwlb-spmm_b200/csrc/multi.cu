@@ -198,14 +198,31 @@ void check_shard_args(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const cwlb_cos
          "shard index outside [0, n_shards)");
 }
 
+// The cut of a shard build: `cut` checked and copied, or (NULL) the modelled
+// cut of cwlb_shard_bounds.
+std::vector<int32_t> build_cut(int32_t n_rows, const int32_t* rowoff, const cwlb_costs& costs,
+                               const int32_t* cut, int32_t n_shards) {
+    std::vector<int32_t> bounds(static_cast<size_t>(n_shards) + 1);
+    if (cut) {
+        need(cut[0] == 0 && cut[n_shards] == n_rows, CWLB_ERR_INVALID_ARGUMENT,
+             "cut must start at 0 and end at n_rows");
+        for (int32_t g = 0; g < n_shards; ++g)
+            need(cut[g] <= cut[g + 1], CWLB_ERR_INVALID_ARGUMENT, "cut must be non-decreasing");
+        std::copy(cut, cut + n_shards + 1, bounds.begin());
+    } else {
+        shard_bounds_host(n_rows, rowoff, costs.C_compute_ns + costs.C_load_ns, costs.C_store_ns,
+                          n_shards, bounds.data());
+    }
+    return bounds;
+}
+
 cwlb_shard* shard_create_host(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                               const int32_t* col, const float* val, const cwlb_costs& costs,
-                              double capacity, int32_t shard, int32_t n_shards) {
+                              double capacity, int32_t shard, int32_t n_shards,
+                              const int32_t* cut = nullptr) {
     CWLB_CUDA(cudaSetDevice(ctx->device));
     validate_offsets(n_rows, nnz, rowoff);
-    std::vector<int32_t> bounds(static_cast<size_t>(n_shards) + 1);
-    shard_bounds_host(n_rows, rowoff, costs.C_compute_ns + costs.C_load_ns, costs.C_store_ns,
-                      n_shards, bounds.data());
+    const std::vector<int32_t> bounds = build_cut(n_rows, rowoff, costs, cut, n_shards);
     cwlb_shard* sh = new_shard(ctx, shard, n_shards, bounds.data(), rowoff);
     try {
         const int32_t e0 = rowoff[sh->row_begin];
@@ -323,13 +340,21 @@ int cwlb_shard_bounds_rebalance(int32_t n_rows, const int32_t* row_offset,
 int cwlb_shard_create(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* row_offset,
                       const int32_t* col_ind, const float* value, const cwlb_costs* costs,
                       double capacity, int32_t shard, int32_t n_shards, cwlb_shard** out) {
+    return cwlb_shard_create_cut(ctx, n_rows, nnz, row_offset, col_ind, value, costs, capacity,
+                                 nullptr, shard, n_shards, out);
+}
+
+int cwlb_shard_create_cut(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* row_offset,
+                          const int32_t* col_ind, const float* value, const cwlb_costs* costs,
+                          double capacity, const int32_t* cut, int32_t shard, int32_t n_shards,
+                          cwlb_shard** out) {
     return cwlb::guarded_multi([&] {
         cwlb::check_shard_args(ctx, n_rows, nnz, costs, shard, n_shards, out);
         *out = nullptr;
         cwlb::need(row_offset && (nnz == 0 || (col_ind && value)), CWLB_ERR_INVALID_ARGUMENT,
                    "null host buffer");
         *out = cwlb::shard_create_host(ctx, n_rows, nnz, row_offset, col_ind, value, *costs,
-                                       capacity, shard, n_shards);
+                                       capacity, shard, n_shards, cut);
     });
 }
 
@@ -358,18 +383,7 @@ int cwlb_shard_create_device_cut(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
                                   cudaMemcpyDeviceToHost, ctx->stream));
         CWLB_CUDA(cudaStreamSynchronize(ctx->stream));
         cwlb::validate_offsets(n_rows, nnz, h.data());
-        std::vector<int32_t> bounds(static_cast<size_t>(n_shards) + 1);
-        if (cut) {
-            cwlb::need(cut[0] == 0 && cut[n_shards] == n_rows, CWLB_ERR_INVALID_ARGUMENT,
-                       "cut must start at 0 and end at n_rows");
-            for (int32_t g = 0; g < n_shards; ++g)
-                cwlb::need(cut[g] <= cut[g + 1], CWLB_ERR_INVALID_ARGUMENT,
-                           "cut must be non-decreasing");
-            std::copy(cut, cut + n_shards + 1, bounds.begin());
-        } else {
-            cwlb::shard_bounds_host(n_rows, h.data(), costs->C_compute_ns + costs->C_load_ns,
-                                    costs->C_store_ns, n_shards, bounds.data());
-        }
+        const std::vector<int32_t> bounds = cwlb::build_cut(n_rows, h.data(), *costs, cut, n_shards);
         cwlb_shard* sh = cwlb::new_shard(ctx, shard, n_shards, bounds.data(), h.data());
         try {
             const int32_t e0 = h[static_cast<size_t>(sh->row_begin)];

@@ -118,6 +118,8 @@ _sig("cwlb_shard_create", [_vp, _i32, _i32, _vp, _vp, _vp, C.POINTER(cwlb_costs)
                            _i32, C.POINTER(_vp)])
 _sig("cwlb_shard_create_device", [_vp, _i32, _i32, _vp, _vp, _vp, C.POINTER(cwlb_costs), _dbl,
                                   _i32, _i32, C.POINTER(_vp)])
+_sig("cwlb_shard_create_cut", [_vp, _i32, _i32, _vp, _vp, _vp, C.POINTER(cwlb_costs), _dbl, _vp,
+                               _i32, _i32, C.POINTER(_vp)])
 _sig("cwlb_shard_bounds_rebalance", [_i32, _vp, C.POINTER(cwlb_costs), _i32, _vp, _vp, _vp])
 _sig("cwlb_shard_create_device_cut", [_vp, _i32, _i32, _vp, _vp, _vp, C.POINTER(cwlb_costs),
                                       _dbl, _vp, _i32, _i32, C.POINTER(_vp)])
@@ -481,12 +483,20 @@ class Shard:
 
     @classmethod
     def from_host(cls, ctx: "Context", csr: CSR, costs: SpmmCostParams, capacity: float,
-                  shard: int, n_shards: int) -> "Shard":
+                  shard: int, n_shards: int, cut=None) -> "Shard":
+        """cut: n_shards + 1 cut points (e.g. from shard_bounds_rebalance);
+        None cuts as shard_bounds."""
         h = _vp()
         c = costs.c()
-        _check(_lib.cwlb_shard_create(ctx.handle, csr.rows, csr.nnz, _p(csr.RowOffset),
-                                      _p(csr.ColInd), _p(csr.Value), C.byref(c), float(capacity),
-                                      shard, n_shards, C.byref(h)))
+        cb = None
+        if cut is not None:
+            cb = np.ascontiguousarray(cut, np.int32)
+            if len(cb) != n_shards + 1:
+                raise ValueError("cut needs n_shards + 1 entries")
+        _check(_lib.cwlb_shard_create_cut(ctx.handle, csr.rows, csr.nnz, _p(csr.RowOffset),
+                                          _p(csr.ColInd), _p(csr.Value), C.byref(c),
+                                          float(capacity), None if cb is None else _p(cb),
+                                          shard, n_shards, C.byref(h)))
         return cls(ctx, h)
 
     @classmethod

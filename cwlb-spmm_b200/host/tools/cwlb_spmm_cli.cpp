@@ -320,7 +320,10 @@ private:
 // library's shard entry points (cwlb_shard_create / cwlb_shard_aggregate_device):
 // GPU g sorts, partitions and aggregates the g-th cost-balanced block of
 // original rows with X replicated; an iteration's time is the largest of the
-// GPUs' event times (all GPUs launch before any is waited for).
+// GPUs' event times (all GPUs launch before any is waited for).  Before the
+// timing loop the cut is re-weighted by the measured shard times
+// (cwlb_shard_bounds_rebalance; CWLB_REBALANCE=R rounds, default 2, 0 keeps
+// the modelled cut).
 class MultiRunner : public RunnerBase {
 public:
     MultiRunner(const std::vector<int>& devices, const CSR& graph,
@@ -343,20 +346,40 @@ public:
         r.capacity = cwlb_capacity_from_s(s, &costs_);
         const int G = static_cast<int>(gpus_.size());
         const int32_t n = static_cast<int32_t>(graph_.RowOffset.size()) - 1;
-        const int32_t nnz = static_cast<int32_t>(graph_.ColInd.size());
-        for (int g = 0; g < G; ++g) {
-            Gpu& d = *gpus_[g];
-            drop_shard(d);
-            cwlb::check(cwlb_shard_create(d.q.ctx(), n, nnz, graph_.RowOffset.data(),
-                                          graph_.ColInd.data(), graph_.Value.data(), &costs_,
-                                          r.capacity, g, G, &d.shard));
-            int64_t nt = 0;
-            cwlb::check(cwlb_shard_info(d.shard, &d.row_begin, &d.row_end, nullptr, &nt, nullptr));
-            r.tasks += static_cast<std::size_t>(nt);
-            d.out.reset(new DeviceArrayOn<float>(d.dev, static_cast<std::size_t>(d.row_end - d.row_begin) * K_));
-        }
         const char* det = std::getenv("CWLB_DETERMINISTIC");
         const uint32_t flags = (det && std::string(det) == "1") ? CWLB_DETERMINISTIC : 0u;
+        // The modelled cut, then up to CWLB_REBALANCE (default 2) cuts
+        // re-weighted by the GPUs' measured shard times; the fastest is kept.
+        std::vector<int32_t> cut(static_cast<std::size_t>(G) + 1), best;
+        cwlb::check(cwlb_shard_bounds(n, graph_.RowOffset.data(), &costs_, G, cut.data()));
+        const char* rb = std::getenv("CWLB_REBALANCE");
+        const int rounds = rb ? std::max(0, std::atoi(rb)) : 2;
+        build(cut, r.capacity);
+        double best_ms = 0.0;
+        for (int k = 0; rounds > 0 && k <= rounds; ++k) {
+            const std::vector<double> t = shard_ms(flags);
+            const double worst = *std::max_element(t.begin(), t.end());
+            if (best.empty() || worst < best_ms) {
+                best = cut;
+                best_ms = worst;
+            }
+            if (k == rounds) break;
+            std::vector<int32_t> next(cut.size());
+            cwlb::check(cwlb_shard_bounds_rebalance(n, graph_.RowOffset.data(), &costs_, G,
+                                                    cut.data(), t.data(), next.data()));
+            if (next == cut) break;
+            cut = next;
+            build(cut, r.capacity);
+        }
+        if (!best.empty() && best != cut) {
+            cut = best;
+            build(cut, r.capacity);
+        }
+        for (auto& dp : gpus_) {
+            int64_t nt = 0;
+            cwlb::check(cwlb_shard_info(dp->shard, nullptr, nullptr, nullptr, &nt, nullptr));
+            r.tasks += static_cast<std::size_t>(nt);
+        }
         double sum = 0.0;
         for (int it = 0; it < LOOPCOUNT; ++it) {
             for (auto& dp : gpus_) {
@@ -392,6 +415,46 @@ public:
     }
 
 private:
+    // Every GPU's shard of `cut` (cwlb_shard_create_cut) and its output rows.
+    void build(const std::vector<int32_t>& cut, double capacity) {
+        const int G = static_cast<int>(gpus_.size());
+        const int32_t n = static_cast<int32_t>(graph_.RowOffset.size()) - 1;
+        const int32_t nnz = static_cast<int32_t>(graph_.ColInd.size());
+        for (int g = 0; g < G; ++g) {
+            Gpu& d = *gpus_[g];
+            drop_shard(d);
+            cwlb::check(cwlb_shard_create_cut(d.q.ctx(), n, nnz, graph_.RowOffset.data(),
+                                              graph_.ColInd.data(), graph_.Value.data(), &costs_,
+                                              capacity, cut.data(), g, G, &d.shard));
+            cwlb::check(cwlb_shard_info(d.shard, &d.row_begin, &d.row_end, nullptr, nullptr, nullptr));
+            d.out.reset(new DeviceArrayOn<float>(d.dev, static_cast<std::size_t>(d.row_end - d.row_begin) * K_));
+        }
+    }
+    // Mean time (ms) of 3 aggregations of every GPU's shard, after one
+    // untimed; all GPUs run at once.
+    std::vector<double> shard_ms(uint32_t flags) {
+        std::vector<double> t;
+        for (int rep = 0; rep < 2; ++rep) {
+            for (auto& dp : gpus_) {
+                Gpu& d = *dp;
+                cudaSetDevice(d.dev);
+                if (rep == 1) cudaEventRecord(d.e0, d.stream());
+                for (int i = 0; i < (rep == 0 ? 1 : 3); ++i)
+                    cwlb::check(cwlb_shard_aggregate_device(d.shard, d.x->p, rows_, K_, d.out->p, flags));
+                if (rep == 1) cudaEventRecord(d.e1, d.stream());
+            }
+        }
+        for (auto& dp : gpus_) {
+            Gpu& d = *dp;
+            cudaSetDevice(d.dev);
+            cudaEventSynchronize(d.e1);
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, d.e0, d.e1);
+            t.push_back(static_cast<double>(ms) / 3.0);
+        }
+        return t;
+    }
+
     template <typename T>
     struct DeviceArrayOn {
         int dev;

@@ -314,15 +314,20 @@ typedef struct cwlb_shard cwlb_shard;
 int cwlb_shard_create(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* row_offset,
                       const int32_t* col_ind, const float* value, const cwlb_costs* costs,
                       double capacity, int32_t shard, int32_t n_shards, cwlb_shard** out);
+/* cwlb_shard_create with the cut given: `cut` holds n_shards + 1 host ints
+ * from 0 to n_rows, non-decreasing (e.g. from cwlb_shard_bounds_rebalance);
+ * NULL cuts as cwlb_shard_bounds. */
+int cwlb_shard_create_cut(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* row_offset,
+                          const int32_t* col_ind, const float* value, const cwlb_costs* costs,
+                          double capacity, const int32_t* cut, int32_t shard, int32_t n_shards,
+                          cwlb_shard** out);
 /* Same, with the whole CSR already in ctx's device memory (one process per
  * GPU, each holding the graph); the block is sorted straight from it. */
 int cwlb_shard_create_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
                              const int32_t* d_row_offset, const int32_t* d_col_ind,
                              const float* d_value, const cwlb_costs* costs, double capacity,
                              int32_t shard, int32_t n_shards, cwlb_shard** out);
-/* cwlb_shard_create_device with the cut given: `cut` holds n_shards + 1
- * host ints from 0 to n_rows, non-decreasing (e.g. from
- * cwlb_shard_bounds_rebalance); NULL cuts as cwlb_shard_bounds. */
+/* cwlb_shard_create_device with the cut given, as cwlb_shard_create_cut. */
 int cwlb_shard_create_device_cut(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
                                  const int32_t* d_row_offset, const int32_t* d_col_ind,
                                  const float* d_value, const cwlb_costs* costs, double capacity,

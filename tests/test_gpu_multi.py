@@ -112,6 +112,28 @@ def test_shards_from_device_memory_match_the_oracle_block_by_block(oracle, rebal
     assert_mean_close(out.cpu().numpy(), ref, cond, what="assembled shards")
 
 
+def test_host_shards_with_a_given_cut_assemble_the_whole_output(oracle):
+    csr, X = _graph(K=32)
+    G = 3
+    cap = cs.capacity_from_s(48, COSTS)
+    cut = cs.shard_bounds_rebalance(csr.RowOffset, COSTS, cs.shard_bounds(csr.RowOffset, COSTS, G),
+                                    [0.6, 1.0, 3.0])
+    with cs.Context(0) as ctx:
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        d_X = torch.from_numpy(X).cuda()
+        out = torch.full((csr.rows, X.shape[1]), float("nan"), device="cuda")
+        for s in range(G):
+            sh = cs.Shard.from_host(ctx, csr, COSTS, cap, s, G, cut=cut)
+            assert (sh.row_begin, sh.row_end) == (cut[s], cut[s + 1])
+            sh.aggregate_device(d_X.data_ptr(), X.shape[0], X.shape[1],
+                                out[sh.row_begin:sh.row_end].data_ptr())
+            torch.cuda.synchronize()
+            sh.close()
+        assert ctx.take_device_errors() == 0
+    ref, cond = _oracle_mean(oracle, csr, X)
+    assert_mean_close(out.cpu().numpy(), ref, cond, what="host shards, given cut")
+
+
 def test_shard_deterministic_flag_gives_identical_outputs():
     csr, X = _graph(K=32)
     with cs.Context(0) as ctx:
@@ -151,6 +173,10 @@ def test_multi_argument_errors():
             with pytest.raises(ValueError, match="cut must"):
                 cs.Shard.from_device(c0, csr.rows, csr.nnz, d_ro.data_ptr(), d_col.data_ptr(),
                                      d_val.data_ptr(), COSTS, 10.0, 0, 2, cut=bad_cut)
+            with pytest.raises(ValueError, match="cut must"):
+                cs.Shard.from_host(c0, csr, COSTS, 10.0, 1, 2, cut=bad_cut)
+        with pytest.raises(ValueError, match="non-decreasing"):
+            cs.Shard.from_host(c0, csr, COSTS, 10.0, 0, 3, cut=[0, 9, 5, csr.rows])
     finally:
         c0.close()
 
