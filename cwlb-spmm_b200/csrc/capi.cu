@@ -212,7 +212,8 @@ void spmm_host_staged(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
             CWLB_CUDA(cudaStreamWaitEvent(ks, ctx->pipe_ready[c], 0));
             CWLB_CUDA(cudaEventRecord(ctx->pipe_t0[c], ks));
             cwlb::launch_spmm_mean(ctx, n_rows, nnz, d_ro, d_col, d_val, d_org, d_H, h_rows, K,
-                                   d_tasks + t0, nt, d_out, cwlb::kFlagOutCleared);
+                                   d_tasks + t0, nt, d_out,
+                                   cwlb::kFlagOutCleared | cwlb::task_variant_flag(ctx, n_tasks, 0));
             CWLB_CUDA(cudaEventRecord(ctx->pipe_t1[c], ks));
             launched[c] = true;
         }
@@ -447,6 +448,12 @@ int cwlb_spmm_mean_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
         check_ctx(ctx);
         require(n_rows >= 0 && nnz >= 0 && h_rows >= 0 && K >= 0 && n_tasks >= 0,
                 CWLB_ERR_INVALID_ARGUMENT, "negative size");
+        require((flags & ~static_cast<uint32_t>(CWLB_ROWS_COVERED | CWLB_DETERMINISTIC |
+                                                CWLB_TASK_PER_WARP | CWLB_TASK_PER_CTA)) == 0,
+                CWLB_ERR_INVALID_ARGUMENT, "unknown flags");
+        require((flags & (CWLB_TASK_PER_WARP | CWLB_TASK_PER_CTA)) !=
+                    (CWLB_TASK_PER_WARP | CWLB_TASK_PER_CTA),
+                CWLB_ERR_INVALID_ARGUMENT, "CWLB_TASK_PER_WARP and CWLB_TASK_PER_CTA exclude each other");
         cwlb::launch_spmm_mean(ctx, n_rows, nnz, d_row_offset, d_col_ind, d_value,
                                d_origin_local, d_H, h_rows, K, d_tasks, n_tasks, d_out, flags);
     });

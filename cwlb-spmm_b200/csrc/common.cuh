@@ -98,6 +98,12 @@ constexpr uint32_t kFlagOutCleared = 1u << 31;
 constexpr uint32_t kFlagSplitZeroed = 1u << 30;
 
 // Launchers implemented in the .cu files (all asynchronous on ctx->stream).
+// The kernel variant for a task list of n_tasks (CWLB_TASK_PER_CTA or
+// CWLB_TASK_PER_WARP): the one `flags` forces, else one CTA per task for at
+// most 128 tasks per SM.  Callers that launch one list in pieces (chunks, a
+// launch order over part of it) pass the whole list's choice to every piece,
+// so that the pieces compute exactly what one launch would.
+uint32_t task_variant_flag(const cwlb_ctx* ctx, int64_t n_tasks, uint32_t flags);
 void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                       const int32_t* col, const float* val, const int32_t* origin,
                       const float* H, int64_t h_rows, int64_t K, const cwlb_task* tasks,

@@ -706,9 +706,13 @@ void plan_aggregate(cwlb_plan* p, const int32_t* origin, const float* H, int64_t
                      p->tasks, p->n_tasks, out, flags, rest, 0);
     CWLB_CUDA(cudaEventRecord(ctx->plan_fork, ctx->stream));
     CWLB_CUDA(cudaStreamWaitEvent(ctx->copy_stream, ctx->plan_fork, 0));
+    // The ungrouped tasks run in the variant the whole list would (their
+    // rows then equal the task kernel's bit for bit).
     launch_spmm_mean(ctx, p->n_rows, p->nnz, p->rowoff, p->col, p->val, origin, H, h_rows, K,
-                     p->tasks, p->n_tasks, out, flags | kFlagOutCleared | kFlagSplitZeroed, rest,
-                     p->n_rest);
+                     p->tasks, p->n_tasks, out,
+                     flags | kFlagOutCleared | kFlagSplitZeroed |
+                         task_variant_flag(ctx, p->n_tasks, flags),
+                     rest, p->n_rest);
     GroupArgs a{};
     a.rowoff = p->rowoff;
     a.origin = origin;

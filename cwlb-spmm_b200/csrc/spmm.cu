@@ -344,6 +344,13 @@ __device__ __forceinline__ void write_zero_row(const SpmmArgs& a, int32_t orig,
 // Rows of a task staged per warp in short-row mode (see launch_spmm_mean).
 constexpr int kStageRows = 128;
 
+// Task lists of at most this many tasks per SM run one CTA per task
+// (spmm_cta_kernel) instead of one warp per task.
+#ifndef CWLB_CTA_TASK_SMS
+#define CWLB_CTA_TASK_SMS 128
+#endif
+constexpr int kCtaTasksPerSm = CWLB_CTA_TASK_SMS;
+
 template <int L, int V, bool kStage, bool kUnit>
 __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
     constexpr int G = VecCfg<L, V>::G;
@@ -469,6 +476,142 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
             }
         }
         if (g == 0) write_row<V>(a, f, q, ok, acc, t, 0);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-per-segment variant: one 8-warp CTA per task, for task lists too short
+// to fill the GPU with one warp per task (a large S, or a small graph).  A
+// single-row task (a hub fragment) is split over all 8·G lane groups of the
+// CTA: each warp reduces its groups with shuffles, then warp 0 adds the eight
+// warp sums from shared memory in warp order and writes the row once.  The
+// rows of a multi-row task go to the warps in turn (row i to warp i mod 8),
+// and inside a warp to lane groups or teams as in spmm_vec_kernel, so every
+// row that spmm_vec_kernel sums with one group in nonzero order (bit-identical
+// to the reference's order) is summed the same way here.
+
+template <int L, int V, bool kUnit>
+__global__ void __launch_bounds__(kThreads) spmm_cta_kernel(SpmmArgs a) {
+    constexpr int G = VecCfg<L, V>::G;
+    constexpr int W = kWarpsPerCta;
+    const int lane = threadIdx.x & 31;
+    const int w = threadIdx.x >> 5;
+    const int64_t slot = blockIdx.x;  // the grid holds exactly n_slots CTAs
+    const int64_t t = a.sched ? static_cast<int64_t>(__ldg(a.sched + slot)) : slot;
+    if (t < 0 || t >= a.n_tasks) {  // an order entry outside the task list
+        if (threadIdx.x == 0) raise_err(a.err, CWLB_DEVERR_ROW_RANGE);
+        return;
+    }
+    cwlb_task tk;
+    if (!load_task(a, t, tk)) return;  // the same task for the whole CTA
+
+    const int g = lane / L;
+    const int lg = lane % L;
+    const unsigned gmask = L == 32 ? 0xffffffffu : (((1u << L) - 1u) << (g * L));
+    const uint32_t K4 = static_cast<uint32_t>(a.K >> 2);
+    const int64_t q0 = static_cast<int64_t>(blockIdx.y) * (L * V);
+    const float4* __restrict__ H4 = reinterpret_cast<const float4*>(a.H);
+    int64_t q[V];
+    bool ok[V];
+    const float4* hq[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        q[i] = q0 + lg + i * L;
+        ok[i] = q[i] < static_cast<int64_t>(K4);
+        hq[i] = H4 + (ok[i] ? q[i] : static_cast<int64_t>(K4) - 1);
+    }
+    const int n_task_rows = tk.row_end - tk.row_start;
+
+    // A whole row with one group per warp (G = 1) stays with one group, so
+    // that it sums in nonzero order as spmm_vec_kernel does; other single-row
+    // tasks are split over the CTA.
+    RowFrag f1;
+    const int st1 = n_task_rows == 1 ? row_fragment(a, tk.row_start, tk, f1) : 2;
+    if (n_task_rows == 1 && !(G == 1 && st1 == 0 && f1.begin == 0 && f1.end == f1.deg)) {
+        __shared__ float4 part[W][L * V];
+        const RowFrag& f = f1;
+        const int st = st1;  // the same for every thread
+        if (st == 1) {
+            if (a.write_empty && threadIdx.x < L) write_zero_row<V>(a, f.orig, q, ok);
+            return;
+        }
+        if (st != 0) return;
+        float4 acc[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        gather_chunks<L, V, L >= 16 && L * V <= 32, kUnit>(
+            a, f.base + f.begin + (w * G + g) * L, f.base + f.end, W * 32, gmask, lg, hq, ok, K4,
+            acc);
+#pragma unroll
+        for (int sh = L; sh < 32; sh <<= 1) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                acc[i].x += __shfl_xor_sync(0xffffffffu, acc[i].x, sh);
+                acc[i].y += __shfl_xor_sync(0xffffffffu, acc[i].y, sh);
+                acc[i].z += __shfl_xor_sync(0xffffffffu, acc[i].z, sh);
+                acc[i].w += __shfl_xor_sync(0xffffffffu, acc[i].w, sh);
+            }
+        }
+        if (g == 0) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) part[w][lg * V + i] = acc[i];
+        }
+        __syncthreads();
+        if (w == 0 && g == 0) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                float4 sum = part[0][lg * V + i];
+                for (int v = 1; v < W; ++v) {
+                    const float4 p = part[v][lg * V + i];
+                    sum.x += p.x;
+                    sum.y += p.y;
+                    sum.z += p.z;
+                    sum.w += p.w;
+                }
+                acc[i] = sum;
+            }
+            write_row<V>(a, f, q, ok, acc, t, 0);
+        }
+        return;
+    }
+
+    // Multi-row task: row i goes to warp i mod W and, inside the warp, to a
+    // team of T groups, T chosen from the task's row count as in
+    // spmm_vec_kernel (T = 1 with at least G rows: every row summed by one
+    // group in nonzero order).
+    int T = 1;
+    if (G > 1) {
+        while (T * 2 * n_task_rows <= G) T *= 2;
+    }
+    const int teams = G / T;
+    const int team = g / T;
+    const int gt = g - team * T;
+    const int team_lanes = T * L;
+    const unsigned tmask = team_lanes == 32 ? 0xffffffffu
+                                            : (((1u << team_lanes) - 1u) << (team * team_lanes));
+    for (int r = tk.row_start + w + team * W; r < tk.row_end; r += teams * W) {
+        RowFrag f;
+        const int st = row_fragment(a, r, tk, f);
+        if (st == 1) {
+            if (a.write_empty && gt == 0) write_zero_row<V>(a, f.orig, q, ok);
+            continue;
+        }
+        if (st != 0) continue;
+        float4 acc[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        gather_chunks<L, V, false, kUnit>(a, f.base + f.begin + gt * L, f.base + f.end,
+                                          team_lanes, gmask, lg, hq, ok, K4, acc);
+        for (int sh = L; sh < team_lanes; sh <<= 1) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                acc[i].x += __shfl_xor_sync(tmask, acc[i].x, sh);
+                acc[i].y += __shfl_xor_sync(tmask, acc[i].y, sh);
+                acc[i].z += __shfl_xor_sync(tmask, acc[i].z, sh);
+                acc[i].w += __shfl_xor_sync(tmask, acc[i].w, sh);
+            }
+        }
+        if (gt == 0) write_row<V>(a, f, q, ok, acc, t, r == tk.row_start ? 0 : 1);
     }
 }
 
@@ -739,9 +882,18 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 template <int L, int V>
-void launch_vec(const SpmmArgs& a, bool stage, cudaStream_t s) {
+void launch_vec(const SpmmArgs& a, bool stage, bool per_cta, cudaStream_t s) {
     const int64_t K4 = a.K >> 2;
     const int64_t tiles = ceil_div(K4, L * V);
+    if (per_cta) {
+        dim3 grid(static_cast<unsigned>(a.n_slots), static_cast<unsigned>(tiles));
+        if (a.val == nullptr) {
+            spmm_cta_kernel<L, V, true><<<grid, kThreads, 0, s>>>(a);
+        } else {
+            spmm_cta_kernel<L, V, false><<<grid, kThreads, 0, s>>>(a);
+        }
+        return;
+    }
     dim3 grid(static_cast<unsigned>(ceil_div(a.n_slots, kWarpsPerCta)),
               static_cast<unsigned>(tiles));
     // Values NULL (every value 1.0): the instances without value loads and
@@ -758,12 +910,12 @@ void launch_vec(const SpmmArgs& a, bool stage, cudaStream_t s) {
 }
 
 template <int L>
-void launch_vec_v(int V, const SpmmArgs& a, bool stage, cudaStream_t s) {
+void launch_vec_v(int V, const SpmmArgs& a, bool stage, bool per_cta, cudaStream_t s) {
     switch (V) {
-        case 1: launch_vec<L, 1>(a, stage, s); break;
-        case 2: launch_vec<L, 2>(a, stage, s); break;
-        case 3: launch_vec<L, 3>(a, stage, s); break;
-        default: launch_vec<L, 4>(a, stage, s); break;
+        case 1: launch_vec<L, 1>(a, stage, per_cta, s); break;
+        case 2: launch_vec<L, 2>(a, stage, per_cta, s); break;
+        case 3: launch_vec<L, 3>(a, stage, per_cta, s); break;
+        default: launch_vec<L, 4>(a, stage, per_cta, s); break;
     }
 }
 
@@ -798,6 +950,14 @@ void pick_vec_shape(int64_t K4, int& L, int& V) {
 }
 
 }  // namespace
+
+uint32_t task_variant_flag(const cwlb_ctx* ctx, int64_t n_tasks, uint32_t flags) {
+    if (flags & (CWLB_TASK_PER_WARP | CWLB_TASK_PER_CTA))
+        return flags & (CWLB_TASK_PER_WARP | CWLB_TASK_PER_CTA);
+    return n_tasks <= static_cast<int64_t>(kCtaTasksPerSm) * ctx->props.multiProcessorCount
+               ? CWLB_TASK_PER_CTA
+               : CWLB_TASK_PER_WARP;
+}
 
 void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                       const int32_t* col, const float* val, const int32_t* origin,
@@ -885,15 +1045,19 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
         // offsets would otherwise be a dependent load on its critical path.
         // It costs 8 KB of shared memory per CTA, taken from L1, so
         // hub-heavy graphs with few rows per task keep the plain kernel.
-        const bool stage = static_cast<int64_t>(n_rows) >= 16 * n_tasks;
+        // One CTA per task when one warp per task would leave the GPU's
+        // last waves to a few long tasks (task_variant_flag); callers that
+        // launch a list in pieces pass the whole list's choice.
+        const bool per_cta = (task_variant_flag(ctx, a.n_tasks, flags) & CWLB_TASK_PER_CTA) != 0;
+        const bool stage = !per_cta && static_cast<int64_t>(n_rows) >= 16 * n_tasks;
         if (stage && a.val == nullptr && nnz > 0) a.val = ones_array(ctx, nnz);
         switch (L) {
-            case 1: launch_vec_v<1>(V, a, stage, s); break;
-            case 2: launch_vec_v<2>(V, a, stage, s); break;
-            case 4: launch_vec_v<4>(V, a, stage, s); break;
-            case 8: launch_vec_v<8>(V, a, stage, s); break;
-            case 16: launch_vec_v<16>(V, a, stage, s); break;
-            default: launch_vec_v<32>(V, a, stage, s); break;
+            case 1: launch_vec_v<1>(V, a, stage, per_cta, s); break;
+            case 2: launch_vec_v<2>(V, a, stage, per_cta, s); break;
+            case 4: launch_vec_v<4>(V, a, stage, per_cta, s); break;
+            case 8: launch_vec_v<8>(V, a, stage, per_cta, s); break;
+            case 16: launch_vec_v<16>(V, a, stage, per_cta, s); break;
+            default: launch_vec_v<32>(V, a, stage, per_cta, s); break;
         }
         CWLB_LAUNCH_CHECK("spmm_vec_kernel");
     } else {

@@ -44,6 +44,8 @@ OK, ERR_INVALID_ARGUMENT, ERR_RUNTIME, ERR_OVERFLOW, ERR_CUDA, ERR_NO_DEVICE, \
     ERR_BUFFER_TOO_SMALL, ERR_OUT_OF_MEMORY = range(8)
 ROWS_COVERED = 1
 DETERMINISTIC = 2
+TASK_PER_WARP = 4
+TASK_PER_CTA = 8
 DEVERR_COL_RANGE, DEVERR_ROW_RANGE, DEVERR_OFFSETS, DEVERR_ORIGIN_RANGE = 1, 2, 4, 8
 
 

@@ -149,6 +149,14 @@ int cwlb_spmm_kernel_large_k(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
  * reference's atomics (src/parallelMatrix.cpp:219-234) promise no order. */
 #define CWLB_ROWS_COVERED 1u
 #define CWLB_DETERMINISTIC 2u
+/* Kernel variant (K a multiple of 4, H and out 16-byte aligned): one warp per
+ * task, or, when the list holds at most 128 tasks per SM (a large S, a small
+ * graph), one 8-warp CTA per task, a hub fragment then split over the CTA and
+ * reduced through shared memory.  Either way a row that one lane group sums
+ * alone is summed in nonzero order, so those rows are bit-identical between
+ * the two.  These flags force one variant (tuning, tests); not both. */
+#define CWLB_TASK_PER_WARP 4u
+#define CWLB_TASK_PER_CTA 8u
 int cwlb_spmm_mean_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
                           const int32_t* d_row_offset, const int32_t* d_col_ind,
                           const float* d_value, const int32_t* d_origin_local, const float* d_H,

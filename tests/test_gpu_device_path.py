@@ -314,3 +314,114 @@ def test_null_values_equal_an_array_of_ones_bit_for_bit(ctx, oracle, K, S):
     for vals in (p["sval"].data_ptr(), 0):
         run(vals, 0, bad_col.data_ptr())
         assert ctx.take_device_errors() & cs.DEVERR_COL_RANGE
+
+
+@pytest.mark.parametrize("K,S", [(32, 512), (64, 1024), (128, 512), (512, 1024), (1100, 2048)])
+def test_cta_per_task_variant_matches_oracle(ctx, oracle, K, S):
+    """A task list of at most 8 tasks per SM runs one CTA per task
+    (spmm_cta_kernel: a hub fragment split over the CTA's eight warps and
+    reduced through shared memory in warp order, the rows of a multi-row task
+    spread over the warps).  Checked against the oracle with weighted and
+    NULL (unit) values, with and without CWLB_ROWS_COVERED; in deterministic
+    mode two runs are bit-identical and NULL values equal an array of ones."""
+    rowoff, col, _ = graphs.rmat_np(13, 150_000, 0.57, 0.19, 0.19, seed=33, symmetrize=True,
+                                    drop_self_loops=True, dedupe=True)
+    n, nnz = len(rowoff) - 1, len(col)
+    rng = np.random.default_rng(34)
+    X = graphs.uniform_features_np(n, K, seed=35)
+    costs = cs.SpmmCostParams(0.02, 0.7, 0.3, 0.5)
+    sms = ctx.device_info()["max_compute_units"]
+    for kind in ("weighted", "unit"):
+        val = (rng.uniform(0.5, 1.5, nnz).astype(np.float32) if kind == "weighted"
+               else np.ones(nnz, np.float32))
+        p = _device_pipeline(ctx, rowoff, col, val, X, costs, S)
+        torch.cuda.synchronize()
+        assert 0 < p["n_tasks"] <= 8 * sms, p["n_tasks"]
+        chk = ctx.tasks_check(n, nnz, p["sro"].data_ptr(), p["t_ptr"], p["n_tasks"])
+        assert chk == dict(bad_tasks=0, uncovered_rows=0, nnz_coverage_errors=0)
+        vptr = p["sval"].data_ptr() if kind == "weighted" else 0
+
+        def run(flags, vals=vptr):
+            out = torch.full((n, K), float("nan"), dtype=torch.float32, device="cuda:0")
+            if not flags & cs.ROWS_COVERED:
+                out.zero_()
+            ctx.spmm_mean_device(n, nnz, p["sro"].data_ptr(), p["scol"].data_ptr(), vals,
+                                 p["org"].data_ptr(), p["X"].data_ptr(), n, K, p["t_ptr"],
+                                 p["n_tasks"], out.data_ptr(), flags)
+            torch.cuda.synchronize()
+            assert ctx.take_device_errors() == 0
+            return out.cpu().numpy()
+
+        ref, cond = oracle.spmm_mean_f64(p["sro"].cpu().numpy(), p["scol"][:nnz].cpu().numpy(),
+                                         p["sval"][:nnz].cpu().numpy(), p["org"].cpu().numpy(), X)
+        for flags in (0, cs.ROWS_COVERED):
+            assert_mean_close(run(flags), ref, cond, what=f"CTA per task, {kind}, K={K}, {flags}")
+        d1, d2 = run(cs.DETERMINISTIC), run(cs.DETERMINISTIC)
+        assert np.array_equal(d1.view(np.uint32), d2.view(np.uint32))
+        assert_mean_close(d1, ref, cond, what=f"CTA per task, {kind}, K={K}, deterministic")
+        if kind == "unit":
+            ones = run(cs.DETERMINISTIC, p["sval"].data_ptr())
+            assert np.array_equal(d1.view(np.uint32), ones.view(np.uint32))
+
+
+@pytest.mark.parametrize("K", [4, 32, 64, 100, 128, 512, 1100])
+@pytest.mark.parametrize("graph", ["short_rows", "hubs"])
+def test_task_variants_agree(ctx, oracle, K, graph):
+    """The same task list through both kernel variants, forced with
+    CWLB_TASK_PER_WARP / CWLB_TASK_PER_CTA: both within the tolerance of the
+    oracle's float64 mean, and every whole row of a task of at least 32 rows
+    (one lane group per row in both, nonzero order) bit-identical between
+    them.  The short-row graph (~100 rows of degree ~4 per task) runs the
+    warp variant's short-row instance."""
+    from helpers import random_csr
+    rng = np.random.default_rng(500 + K)
+    if graph == "short_rows":
+        d = rng.integers(1, 8, 20_000)
+        rowoff = np.zeros(len(d) + 1, np.int32)
+        rowoff[1:] = np.cumsum(d)
+        col = rng.integers(0, 20_000, int(rowoff[-1])).astype(np.int32)
+        val = rng.uniform(0.5, 1.5, len(col)).astype(np.float32)
+        n_cols, S = 20_000, 300
+    else:
+        rowoff, col, val = random_csr(rng, 5000, 60, n_cols=4000, hubs=6, hub_factor=80)
+        n_cols, S = 4000, 48
+    n, nnz = len(rowoff) - 1, len(col)
+    X = rng.standard_normal((n_cols, K)).astype(np.float32)
+    costs = cs.SpmmCostParams(0.02, 0.7, 0.3, 0.5)
+    p = _device_pipeline(ctx, rowoff, col, val, X, costs, S)
+    torch.cuda.synchronize()
+
+    def run(flags):
+        out = torch.full((n, K), float("nan"), dtype=torch.float32, device="cuda:0")
+        ctx.spmm_mean_device(n, nnz, p["sro"].data_ptr(), p["scol"].data_ptr(),
+                             p["sval"].data_ptr(), p["org"].data_ptr(), p["X"].data_ptr(), n_cols,
+                             K, p["t_ptr"], p["n_tasks"], out.data_ptr(),
+                             cs.ROWS_COVERED | flags)
+        torch.cuda.synchronize()
+        assert ctx.take_device_errors() == 0
+        return out.cpu().numpy()
+
+    warp, cta = run(cs.TASK_PER_WARP), run(cs.TASK_PER_CTA)
+    o = [t.cpu().numpy() for t in (p["sro"], p["scol"][:nnz], p["sval"][:nnz], p["org"])]
+    ref, cond = oracle.spmm_mean_f64(o[0], o[1], o[2], o[3], X)
+    assert_mean_close(warp, ref, cond, what=f"warp per task, K={K}, {graph}")
+    assert_mean_close(cta, ref, cond, what=f"CTA per task, K={K}, {graph}")
+    tasks = torch.as_tensor(_DevTasks(p["t_ptr"], p["n_tasks"]), device="cuda:0").cpu().numpy()
+    deg = np.diff(o[0])
+    rows = []
+    for rs, re_, fo, ln in tasks.reshape(-1, 4):
+        if re_ - rs < 32:
+            continue
+        for r in range(rs, re_):
+            b = fo if r == rs else 0
+            e = ln if (r == re_ - 1 and ln > 0) else deg[r]
+            if b == 0 and e == deg[r]:
+                rows.append(o[3][r])
+    if graph == "short_rows":
+        assert len(rows) > n // 2
+    rows = np.array(rows, np.int64)
+    assert np.array_equal(warp[rows].view(np.uint32), cta[rows].view(np.uint32))
+    with pytest.raises(ValueError):
+        run(cs.TASK_PER_WARP | cs.TASK_PER_CTA)
+    with pytest.raises(ValueError):
+        run(1 << 30)
