@@ -93,16 +93,20 @@ namespace cwlb {
 
 // launch_spmm_mean flag (internal): the caller has already zeroed `out`.
 constexpr uint32_t kFlagOutCleared = 1u << 31;
+// Warp kernels (one warp per task, or per run of small tasks), not one CTA
+// per task: what task_variant_flag gives a long task list.
+constexpr uint32_t kFlagWarpTasks = 1u << 29;
 // launch_spmm_mean flag (internal): the split rows of a CWLB_ROWS_COVERED call
 // have already been zeroed (by an earlier call with n_slots == 0).
 constexpr uint32_t kFlagSplitZeroed = 1u << 30;
 
 // Launchers implemented in the .cu files (all asynchronous on ctx->stream).
-// The kernel variant for a task list of n_tasks (CWLB_TASK_PER_CTA or
-// CWLB_TASK_PER_WARP): the one `flags` forces, else one CTA per task for at
-// most 128 tasks per SM.  Callers that launch one list in pieces (chunks, a
-// launch order over part of it) pass the whole list's choice to every piece,
-// so that the pieces compute exactly what one launch would.
+// The kernel family for a task list of n_tasks: the one `flags` forces
+// (CWLB_TASK_PER_WARP, CWLB_TASK_PER_CTA), else CWLB_TASK_PER_CTA for at most
+// 128 tasks per SM and kFlagWarpTasks otherwise.  Callers that launch one list
+// in pieces (chunks, a launch order over part of it) pass the whole list's
+// choice to every piece, so that every row a task covers whole comes out as
+// one launch would give it.
 uint32_t task_variant_flag(const cwlb_ctx* ctx, int64_t n_tasks, uint32_t flags);
 void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                       const int32_t* col, const float* val, const int32_t* origin,

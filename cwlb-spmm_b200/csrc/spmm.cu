@@ -70,6 +70,8 @@ struct SpmmArgs {
     // index into [0, n_tasks); nullptr runs task i for every i < n_tasks.
     const int32_t* __restrict__ sched;
     int64_t n_slots;
+    // spmm_run_kernel: consecutive tasks per warp.
+    int32_t run;
 };
 
 __device__ __forceinline__ void raise_err(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
@@ -351,6 +353,14 @@ constexpr int kStageRows = 128;
 #endif
 constexpr int kCtaTasksPerSm = CWLB_CTA_TASK_SMS;
 
+// Task lists averaging fewer than kRunMaxTaskNnz nonzeros a task run as warp
+// runs of about kRunNnz nonzeros (spmm_run_kernel).
+#ifndef CWLB_RUN_NNZ
+#define CWLB_RUN_NNZ 512
+#endif
+constexpr int64_t kRunNnz = CWLB_RUN_NNZ;
+constexpr int64_t kRunMaxTaskNnz = 128;
+
 template <int L, int V, bool kStage, bool kUnit>
 __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
     constexpr int G = VecCfg<L, V>::G;
@@ -477,6 +487,139 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
         }
         if (g == 0) write_row<V>(a, f, q, ok, acc, t, 0);
     }
+}
+
+// ---------------------------------------------------------------------------
+// Runs of small tasks (a small S): one warp per run of a.run consecutive
+// tasks.  Consecutive single-row tasks over adjacent nonzeros of the same row
+// (a hub row cut into many S-nonzero fragments) accumulate in the warp's
+// registers and reach the output with one write per run, an atomic add
+// unless the run covers the whole row: a.run times fewer atomics, and a.run
+// times less rounding from adding thousands of fragments to one output row
+// in float (at S = 16 a row of degree 10^6 receives 62,500 adds).  Every other
+// task runs exactly as in spmm_vec_kernel (same lane groups, teams and
+// nonzero order), so every row that a single task covers whole is
+// bit-identical between the two kernels.
+
+template <int L, int V, bool kUnit>
+__global__ void __launch_bounds__(kThreads) spmm_run_kernel(SpmmArgs a) {
+    constexpr int G = VecCfg<L, V>::G;
+    constexpr bool kPf = L >= 16 && L * V <= 32;
+    const int lane = threadIdx.x & 31;
+    const int64_t wi = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
+    const int64_t t_begin = wi * a.run;
+    if (t_begin >= a.n_tasks) return;
+    const int64_t t_end = min(t_begin + static_cast<int64_t>(a.run), a.n_tasks);
+
+    const int g = lane / L;
+    const int lg = lane % L;
+    const unsigned gmask = L == 32 ? 0xffffffffu : (((1u << L) - 1u) << (g * L));
+    const uint32_t K4 = static_cast<uint32_t>(a.K >> 2);
+    const int64_t q0 = static_cast<int64_t>(blockIdx.y) * (L * V);
+    const float4* __restrict__ H4 = reinterpret_cast<const float4*>(a.H);
+    int64_t q[V];
+    bool ok[V];
+    const float4* hq[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        q[i] = q0 + lg + i * L;
+        ok[i] = q[i] < static_cast<int64_t>(K4);
+        hq[i] = H4 + (ok[i] ? q[i] : static_cast<int64_t>(K4) - 1);
+    }
+
+    // The carried row: sums of consecutive single-row tasks on sorted row
+    // c_row, nonzeros [cf.begin, cf.end) of it so far.
+    float4 cacc[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) cacc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    RowFrag cf{};
+    int32_t c_row = -1;
+    int64_t c_task = 0;
+    auto flush = [&]() {  // warp-uniform
+        if (c_row < 0) return;
+#pragma unroll
+        for (int sh = L; sh < 32; sh <<= 1) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                cacc[i].x += __shfl_xor_sync(0xffffffffu, cacc[i].x, sh);
+                cacc[i].y += __shfl_xor_sync(0xffffffffu, cacc[i].y, sh);
+                cacc[i].z += __shfl_xor_sync(0xffffffffu, cacc[i].z, sh);
+                cacc[i].w += __shfl_xor_sync(0xffffffffu, cacc[i].w, sh);
+            }
+        }
+        if (g == 0) write_row<V>(a, cf, q, ok, cacc, c_task, 0);
+#pragma unroll
+        for (int i = 0; i < V; ++i) cacc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        c_row = -1;
+    };
+
+    for (int64_t t = t_begin; t < t_end; ++t) {
+        cwlb_task tk;
+        if (!load_task(a, t, tk)) continue;
+        const int n_task_rows = tk.row_end - tk.row_start;
+        if (n_task_rows == 1) {
+            // One row: the G groups take interleaved chunks (as in
+            // spmm_vec_kernel), into the carried sums when the task continues
+            // the carried row.
+            RowFrag f;
+            const int st = row_fragment(a, tk.row_start, tk, f);
+            if (st == 0) {
+                if (c_row != tk.row_start || f.begin != cf.end) {
+                    flush();
+                    cf = f;
+                    c_row = tk.row_start;
+                    c_task = t;
+                } else {
+                    cf.end = f.end;
+                    cf.begin = -1;  // several tasks: added atomically onto the zeroed row
+                }
+                gather_chunks<L, V, kPf, kUnit>(a, f.base + f.begin + g * L, f.base + f.end, 32,
+                                                gmask, lg, hq, ok, K4, cacc);
+                continue;
+            }
+            flush();
+            if (st == 1 && a.write_empty && g == 0) write_zero_row<V>(a, f.orig, q, ok);
+            continue;
+        }
+        flush();
+        // Several rows: teams of T groups, as in spmm_vec_kernel.
+        int T = 1;
+        if (G > 1) {
+            while (T * 2 * n_task_rows <= G) T *= 2;
+        }
+        const int teams = G / T;
+        const int team = g / T;
+        const int gt = g - team * T;
+        const int team_lanes = T * L;
+        const unsigned tmask = team_lanes == 32 ? 0xffffffffu
+                                                : (((1u << team_lanes) - 1u) << (team * team_lanes));
+        for (int r = tk.row_start + team; r < tk.row_end; r += teams) {
+            RowFrag f;
+            const int st = row_fragment(a, r, tk, f);
+            if (st == 1) {
+                if (a.write_empty && gt == 0) write_zero_row<V>(a, f.orig, q, ok);
+                continue;
+            }
+            if (st != 0) continue;
+            // The carry is empty here (flushed above): its registers hold
+            // this row's sums.
+            gather_chunks<L, V, kPf, kUnit>(a, f.base + f.begin + gt * L, f.base + f.end,
+                                            team_lanes, gmask, lg, hq, ok, K4, cacc);
+            for (int sh = L; sh < team_lanes; sh <<= 1) {
+#pragma unroll
+                for (int i = 0; i < V; ++i) {
+                    cacc[i].x += __shfl_xor_sync(tmask, cacc[i].x, sh);
+                    cacc[i].y += __shfl_xor_sync(tmask, cacc[i].y, sh);
+                    cacc[i].z += __shfl_xor_sync(tmask, cacc[i].z, sh);
+                    cacc[i].w += __shfl_xor_sync(tmask, cacc[i].w, sh);
+                }
+            }
+            if (gt == 0) write_row<V>(a, f, q, ok, cacc, t, r == tk.row_start ? 0 : 1);
+#pragma unroll
+            for (int i = 0; i < V; ++i) cacc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    flush();
 }
 
 // ---------------------------------------------------------------------------
@@ -885,6 +1028,16 @@ template <int L, int V>
 void launch_vec(const SpmmArgs& a, bool stage, bool per_cta, cudaStream_t s) {
     const int64_t K4 = a.K >> 2;
     const int64_t tiles = ceil_div(K4, L * V);
+    if (a.run > 1) {
+        dim3 grid(static_cast<unsigned>(ceil_div(ceil_div(a.n_tasks, a.run), kWarpsPerCta)),
+                  static_cast<unsigned>(tiles));
+        if (a.val == nullptr) {
+            spmm_run_kernel<L, V, true><<<grid, kThreads, 0, s>>>(a);
+        } else {
+            spmm_run_kernel<L, V, false><<<grid, kThreads, 0, s>>>(a);
+        }
+        return;
+    }
     if (per_cta) {
         dim3 grid(static_cast<unsigned>(a.n_slots), static_cast<unsigned>(tiles));
         if (a.val == nullptr) {
@@ -952,11 +1105,11 @@ void pick_vec_shape(int64_t K4, int& L, int& V) {
 }  // namespace
 
 uint32_t task_variant_flag(const cwlb_ctx* ctx, int64_t n_tasks, uint32_t flags) {
-    if (flags & (CWLB_TASK_PER_WARP | CWLB_TASK_PER_CTA))
-        return flags & (CWLB_TASK_PER_WARP | CWLB_TASK_PER_CTA);
+    if (flags & (CWLB_TASK_PER_WARP | CWLB_TASK_PER_CTA | kFlagWarpTasks))
+        return flags & (CWLB_TASK_PER_WARP | CWLB_TASK_PER_CTA | kFlagWarpTasks);
     return n_tasks <= static_cast<int64_t>(kCtaTasksPerSm) * ctx->props.multiProcessorCount
                ? CWLB_TASK_PER_CTA
-               : CWLB_TASK_PER_WARP;
+               : kFlagWarpTasks;
 }
 
 void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
@@ -1050,6 +1203,13 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
         // launch a list in pieces pass the whole list's choice.
         const bool per_cta = (task_variant_flag(ctx, a.n_tasks, flags) & CWLB_TASK_PER_CTA) != 0;
         const bool stage = !per_cta && static_cast<int64_t>(n_rows) >= 16 * n_tasks;
+        // Small tasks (a small S; not forced to one warp per task): runs of
+        // tasks per warp, about kRunNnz nonzeros a run, at most 32 tasks.
+        if (!per_cta && !stage && !sched && !det && !(flags & CWLB_TASK_PER_WARP)) {
+            const int64_t per_task = std::max<int64_t>(1, nnz / n_tasks);
+            if (per_task < kRunMaxTaskNnz)
+                a.run = static_cast<int32_t>(std::min<int64_t>(32, std::max<int64_t>(2, kRunNnz / per_task)));
+        }
         if (stage && a.val == nullptr && nnz > 0) a.val = ones_array(ctx, nnz);
         switch (L) {
             case 1: launch_vec_v<1>(V, a, stage, per_cta, s); break;

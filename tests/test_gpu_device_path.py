@@ -425,3 +425,51 @@ def test_task_variants_agree(ctx, oracle, K, graph):
         run(cs.TASK_PER_WARP | cs.TASK_PER_CTA)
     with pytest.raises(ValueError):
         run(1 << 30)
+
+
+@pytest.mark.parametrize("K,S", [(32, 8), (64, 16), (128, 32), (512, 16), (1100, 64)])
+def test_task_runs_match_one_warp_per_task(ctx, oracle, K, S):
+    """Small tasks (fewer than 128 nonzeros on average, a long list) run as
+    warp runs of consecutive tasks (spmm_run_kernel): consecutive fragments of
+    one row are summed in registers and written once.  Against the same list
+    forced to one warp per task (CWLB_TASK_PER_WARP): both within the
+    tolerance of the oracle's float64 mean, and every row one task covers
+    whole bit-identical between them."""
+    rowoff, col, _ = graphs.rmat_np(15, 1_200_000, 0.6, 0.15, 0.15, seed=37, symmetrize=True,
+                                    drop_self_loops=True, dedupe=True)
+    n, nnz = len(rowoff) - 1, len(col)
+    rng = np.random.default_rng(38)
+    val = rng.uniform(0.5, 1.5, nnz).astype(np.float32)
+    X = graphs.uniform_features_np(n, K, seed=39)
+    costs = cs.SpmmCostParams(0.02, 0.7, 0.3, 0.5)
+    p = _device_pipeline(ctx, rowoff, col, val, X, costs, S)
+    torch.cuda.synchronize()
+    sms = ctx.device_info()["max_compute_units"]
+    assert p["n_tasks"] > 128 * sms and nnz / p["n_tasks"] < 128 and n < 16 * p["n_tasks"]
+
+    def run(flags):
+        out = torch.full((n, K), float("nan"), dtype=torch.float32, device="cuda:0")
+        ctx.spmm_mean_device(n, nnz, p["sro"].data_ptr(), p["scol"].data_ptr(),
+                             p["sval"].data_ptr(), p["org"].data_ptr(), p["X"].data_ptr(), n, K,
+                             p["t_ptr"], p["n_tasks"], out.data_ptr(), cs.ROWS_COVERED | flags)
+        torch.cuda.synchronize()
+        assert ctx.take_device_errors() == 0
+        return out.cpu().numpy()
+
+    runs, warp = run(0), run(cs.TASK_PER_WARP)
+    o = [t.cpu().numpy() for t in (p["sro"], p["scol"][:nnz], p["sval"][:nnz], p["org"])]
+    ref, cond = oracle.spmm_mean_f64(o[0], o[1], o[2], o[3], X)
+    assert_mean_close(runs, ref, cond, what=f"task runs, K={K}, S={S}")
+    assert_mean_close(warp, ref, cond, what=f"warp per task, K={K}, S={S}")
+    tasks = torch.as_tensor(_DevTasks(p["t_ptr"], p["n_tasks"]), device="cuda:0").cpu().numpy()
+    deg = np.diff(o[0])
+    whole = []
+    for rs, re_, fo, ln in tasks.reshape(-1, 4):
+        for r in range(rs, re_):
+            b = fo if r == rs else 0
+            e = ln if (r == re_ - 1 and ln > 0) else deg[r]
+            if b == 0 and e == deg[r]:
+                whole.append(o[3][r])
+    whole = np.array(whole, np.int64)
+    assert len(whole) > n // 4
+    assert np.array_equal(runs[whole].view(np.uint32), warp[whole].view(np.uint32))
