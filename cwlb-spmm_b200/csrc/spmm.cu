@@ -356,7 +356,7 @@ constexpr int kCtaTasksPerSm = CWLB_CTA_TASK_SMS;
 // Task lists averaging fewer than kRunMaxTaskNnz nonzeros a task run as warp
 // runs of about kRunNnz nonzeros (spmm_run_kernel).
 #ifndef CWLB_RUN_NNZ
-#define CWLB_RUN_NNZ 512
+#define CWLB_RUN_NNZ 2048
 #endif
 constexpr int64_t kRunNnz = CWLB_RUN_NNZ;
 constexpr int64_t kRunMaxTaskNnz = 128;
