@@ -150,11 +150,15 @@ int cwlb_spmm_kernel_large_k(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
 #define CWLB_ROWS_COVERED 1u
 #define CWLB_DETERMINISTIC 2u
 /* Kernel variant (K a multiple of 4, H and out 16-byte aligned): one warp per
- * task, or, when the list holds at most 128 tasks per SM (a large S, a small
+ * task; when the list holds at most 128 tasks per SM (a large S, a small
  * graph), one 8-warp CTA per task, a hub fragment then split over the CTA and
- * reduced through shared memory.  Either way a row that one lane group sums
- * alone is summed in nonzero order, so those rows are bit-identical between
- * the two.  These flags force one variant (tuning, tests); not both. */
+ * reduced through shared memory; when tasks average fewer than 128 nonzeros
+ * (a small S), one warp per run of consecutive tasks, consecutive fragments
+ * of one row summed in registers and written once (fewer float atomics, less
+ * rounding).  A row that one lane group sums alone is summed in nonzero order
+ * in every variant, so those rows are bit-identical between them.  These
+ * flags force one warp per task (no runs) or one CTA per task (tuning,
+ * tests); not both. */
 #define CWLB_TASK_PER_WARP 4u
 #define CWLB_TASK_PER_CTA 8u
 int cwlb_spmm_mean_device(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz,
