@@ -10,17 +10,20 @@ step) with HBM GB/s against the measured roofline.
   python bench.py --impl reference ...   (the CPU implementation of the path)
 
 Multi-GPU (torchrun, one rank per GPU): every rank builds the same graph and
-hands it to the library's shard entry point (cwlb_shard_create_device), which
-takes a contiguous, cost-balanced block of ORIGINAL rows (X replicated), sorts
-and partitions it on the rank's GPU; each step aggregates the block
-(cwlb_shard_aggregate_device); no collective on the data path.  Total work
+hands it to the library's shard entry point (cwlb_shard_create_device_cut),
+which takes a contiguous, cost-balanced block of ORIGINAL rows (X replicated),
+sorts and partitions it on the rank's GPU; each step aggregates the block
+(cwlb_shard_aggregate_device); no collective on the data path.  Before the
+timed region the cut is re-weighted by the ranks' measured shard times
+(cwlb_shard_bounds_rebalance, --rebalance rounds; the times are all-gathered
+so that every rank computes the same cut).  Total work
 is fixed as N grows ("strong" scaling).  With --x-sharded, X starts
 row-sharded (each rank holds the rows it owns, as a prior layer's output
 leaves it) and every timed step all-gathers it over NCCL first.
 
 Outside the timed region: graph synthesis (torch, seeded), degree sort,
 partition (both on the GPU), the S choice (the reference's --candidates
-procedure), task validation.  Inside: the aggregation launches only
+procedure), task validation, the shard re-cut.  Inside: the aggregation launches only
 (device-resident value); `e2e` times the host-buffer C-ABI call
 (cwlb_spmm_kernel) with the H2D copy of every input and the D2H copy of the
 output inside each step.
