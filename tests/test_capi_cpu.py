@@ -26,6 +26,23 @@ def test_library_exports_every_header_function():
     assert not missing, f"declared but not exported: {missing}"
 
 
+def test_python_constants_equal_the_header_defines():
+    """The binding's flag and status constants are the header's #defines."""
+    import re
+    with open(cs.HEADER_PATH) as fh:
+        text = fh.read()
+    defines = {m.group(1): int(m.group(2), 0)
+               for m in re.finditer(r"#define\s+CWLB_(\w+)\s+\(?([0-9xXa-fA-F]+)u?", text)}
+    checked = 0
+    for name, value in defines.items():
+        if hasattr(cs, name):
+            assert getattr(cs, name) == value, name
+            checked += 1
+    for name in ("ROWS_COVERED", "DETERMINISTIC", "TASK_PER_WARP", "TASK_PER_CTA"):
+        assert name in defines and getattr(cs, name) == defines[name], name
+    assert checked >= 6
+
+
 def test_context_without_device_fails_loudly():
     try:
         import torch
