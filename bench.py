@@ -79,7 +79,7 @@ def parse_args():
                     help="N = 1: time an aggregation plan (cwlb_plan_*, built outside the timed "
                          "region) with this group size (0 = the library's choice) instead of "
                          "the task kernel")
-    ap.add_argument("--rebalance", type=int, default=2, metavar="ROUNDS",
+    ap.add_argument("--rebalance", type=int, default=4, metavar="ROUNDS",
                     help="N > 1: re-cut the shards up to ROUNDS times by their measured "
                          "aggregation times (cwlb_shard_bounds_rebalance), before the timed "
                          "region; 0 keeps the cost-model cut")

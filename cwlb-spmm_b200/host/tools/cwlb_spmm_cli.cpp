@@ -322,7 +322,7 @@ private:
 // original rows with X replicated; an iteration's time is the largest of the
 // GPUs' event times (all GPUs launch before any is waited for).  Before the
 // timing loop the cut is re-weighted by the measured shard times
-// (cwlb_shard_bounds_rebalance; CWLB_REBALANCE=R rounds, default 2, 0 keeps
+// (cwlb_shard_bounds_rebalance; CWLB_REBALANCE=R rounds, default 4, 0 keeps
 // the modelled cut).
 class MultiRunner : public RunnerBase {
 public:
@@ -348,12 +348,12 @@ public:
         const int32_t n = static_cast<int32_t>(graph_.RowOffset.size()) - 1;
         const char* det = std::getenv("CWLB_DETERMINISTIC");
         const uint32_t flags = (det && std::string(det) == "1") ? CWLB_DETERMINISTIC : 0u;
-        // The modelled cut, then up to CWLB_REBALANCE (default 2) cuts
+        // The modelled cut, then up to CWLB_REBALANCE (default 4) cuts
         // re-weighted by the GPUs' measured shard times; the fastest is kept.
         std::vector<int32_t> cut(static_cast<std::size_t>(G) + 1), best;
         cwlb::check(cwlb_shard_bounds(n, graph_.RowOffset.data(), &costs_, G, cut.data()));
         const char* rb = std::getenv("CWLB_REBALANCE");
-        const int rounds = rb ? std::max(0, std::atoi(rb)) : 2;
+        const int rounds = rb ? std::max(0, std::atoi(rb)) : 4;
         build(cut, r.capacity);
         double best_ms = 0.0;
         for (int k = 0; rounds > 0 && k <= rounds; ++k) {
