@@ -352,7 +352,7 @@ int cwlb_ctx_destroy(cwlb_ctx* ctx) {
         for (cwlb::DeviceBuffer* b : {&ctx->in_rowoff, &ctx->in_col, &ctx->in_val, &ctx->in_origin,
                                       &ctx->in_H, &ctx->in_tasks, &ctx->out_buf, &ctx->sort_scratch,
                                       &ctx->part_scratch, &ctx->part_desc, &ctx->part_tasks,
-                                      &ctx->check_scratch, &ctx->ones, &ctx->det_scratch})
+                                      &ctx->check_scratch, &ctx->det_scratch})
             b->release();
         if (ctx->d_error_flags) cudaFree(ctx->d_error_flags);
         if (ctx->copy_stream) cudaStreamSynchronize(ctx->copy_stream);

@@ -80,9 +80,6 @@ struct cwlb_ctx {
     // device) and for the sort / partition pipelines.
     cwlb::DeviceBuffer in_rowoff, in_col, in_val, in_origin, in_H, in_tasks, out_buf;
     cwlb::DeviceBuffer sort_scratch, part_scratch, part_desc, part_tasks, check_scratch;
-    // 1.0f values for kernels that are given NULL values but read values.
-    cwlb::DeviceBuffer ones;
-    size_t ones_count = 0;
     // Fragment partials and their plan (CWLB_DETERMINISTIC).
     cwlb::DeviceBuffer det_scratch;
     // Created by the first large copy of pageable caller memory.
@@ -131,8 +128,6 @@ void plan_destroy(cwlb_plan* p);
 // (synchronous; d_flag is one word of device scratch) (spmm.cu).  Kernels
 // given NULL values treat every value as 1.0f.
 bool values_all_one(cwlb_ctx* ctx, const float* d_val, size_t count, unsigned int* d_flag);
-// `count` floats of 1.0f owned by the context (filled once, on its stream).
-const float* ones_array(cwlb_ctx* ctx, int32_t count);
 // Float64 reference of the aggregation over an unsorted CSR (spmm.cu).
 void launch_spmm_mean_reference(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                                 const int32_t* col, const float* val, const float* H,

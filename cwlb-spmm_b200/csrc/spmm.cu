@@ -343,8 +343,6 @@ __device__ __forceinline__ void write_zero_row(const SpmmArgs& a, int32_t orig,
         if (ok[i]) __stcs(out4 + q[i], make_float4(0.f, 0.f, 0.f, 0.f));
 }
 
-// Rows of a task staged per warp in short-row mode (see launch_spmm_mean).
-constexpr int kStageRows = 128;
 
 // Task lists of at most this many tasks per SM run one CTA per task
 // (spmm_cta_kernel) instead of one warp per task.
@@ -352,6 +350,14 @@ constexpr int kStageRows = 128;
 #define CWLB_CTA_TASK_SMS 128
 #endif
 constexpr int kCtaTasksPerSm = CWLB_CTA_TASK_SMS;
+
+// Short-row mode (windows of row offsets and origins held in registers and
+// shared by shuffles) for task lists averaging at least this many rows a task.
+#ifndef CWLB_STAGE_ROWS
+#define CWLB_STAGE_ROWS 16
+#endif
+constexpr int64_t kStageRowsPerTask = CWLB_STAGE_ROWS;
+
 
 // Task lists averaging fewer than kRunMaxTaskNnz nonzeros a task run as warp
 // runs of about kRunNnz nonzeros (spmm_run_kernel).
@@ -408,57 +414,73 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
         const int team_lanes = T * L;
         const unsigned tmask = team_lanes == 32 ? 0xffffffffu
                                                 : (((1u << team_lanes) - 1u) << (team * team_lanes));
-        // Short-row mode: the task's row offsets and origins are loaded with a
-        // few coalesced loads up front, so that no row waits on its own.
-        struct Staged {
-            int32_t ro[kWarpsPerCta][kStageRows + 1];
-            int32_t org[kWarpsPerCta][kStageRows];
-        };
-        __shared__ typename std::conditional<kStage, Staged, char>::type stage;
-        const int w = threadIdx.x >> 5;
-        bool staged = false;
+        constexpr bool kPf = L >= 16 && L * V <= 32;
         if constexpr (kStage) {
-            staged = n_task_rows <= kStageRows;
-            if (staged) {
-                for (int i = lane; i <= n_task_rows; i += 32)
-                    stage.ro[w][i] = __ldg(a.rowoff + tk.row_start + i);
-                for (int i = lane; i < n_task_rows; i += 32)
-                    stage.org[w][i] = __ldg(a.origin + tk.row_start + i);
-                __syncwarp();
-            }
-        }
-        for (int r = tk.row_start + team; r < tk.row_end; r += teams) {
-            RowFrag f;
-            int st;
-            if constexpr (kStage) {
-                const int i = r - tk.row_start;
-                st = staged ? row_fragment_at(a, r, tk, stage.ro[w][i], stage.ro[w][i + 1],
-                                              stage.org[w][i], f)
-                            : row_fragment(a, r, tk, f);
-            } else {
-                (void)w;
-                st = row_fragment(a, r, tk, f);
-            }
-            if (st == 1) {
-                if (a.write_empty && gt == 0) write_zero_row<V>(a, f.orig, q, ok);
-                continue;
-            }
-            if (st != 0) continue;
-            float4 acc[V];
+            // Short-row mode: rows in windows of 31.  Lane i loads the offset
+            // and origin of the window's row i with one coalesced load each;
+            // each row's team takes them by shuffle, so no row waits on its
+            // own dependent offset loads.
+            for (int wb = tk.row_start; wb < tk.row_end; wb += 31) {
+                const int wn = min(31, tk.row_end - wb);
+                const int32_t w_ro = lane <= wn ? __ldg(a.rowoff + wb + lane) : 0;
+                const int32_t w_org = lane < wn ? __ldg(a.origin + wb + lane) : 0;
+                for (int i0 = 0; i0 < wn; i0 += teams) {  // warp-uniform
+                    const int i = i0 + team;
+                    const int src = min(i, 30);
+                    const int32_t b0 = __shfl_sync(0xffffffffu, w_ro, src);
+                    const int32_t b1 = __shfl_sync(0xffffffffu, w_ro, src + 1);
+                    const int32_t og = __shfl_sync(0xffffffffu, w_org, src);
+                    if (i >= wn) continue;
+                    const int r = wb + i;
+                    RowFrag f;
+                    const int st = row_fragment_at(a, r, tk, b0, b1, og, f);
+                    if (st == 1) {
+                        if (a.write_empty && gt == 0) write_zero_row<V>(a, f.orig, q, ok);
+                        continue;
+                    }
+                    if (st != 0) continue;
+                    float4 acc[V];
 #pragma unroll
-            for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            gather_chunks<L, V, !kStage && L >= 16 && L * V <= 32, kUnit>(a, f.base + f.begin + gt * L, f.base + f.end, team_lanes, gmask, lg,
-                                hq, ok, K4, acc);
-            for (int sh = L; sh < team_lanes; sh <<= 1) {
+                    for (int k = 0; k < V; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    gather_chunks<L, V, kPf, kUnit>(a, f.base + f.begin + gt * L, f.base + f.end,
+                                                    team_lanes, gmask, lg, hq, ok, K4, acc);
+                    for (int sh = L; sh < team_lanes; sh <<= 1) {
 #pragma unroll
-                for (int i = 0; i < V; ++i) {
-                    acc[i].x += __shfl_xor_sync(tmask, acc[i].x, sh);
-                    acc[i].y += __shfl_xor_sync(tmask, acc[i].y, sh);
-                    acc[i].z += __shfl_xor_sync(tmask, acc[i].z, sh);
-                    acc[i].w += __shfl_xor_sync(tmask, acc[i].w, sh);
+                        for (int k = 0; k < V; ++k) {
+                            acc[k].x += __shfl_xor_sync(tmask, acc[k].x, sh);
+                            acc[k].y += __shfl_xor_sync(tmask, acc[k].y, sh);
+                            acc[k].z += __shfl_xor_sync(tmask, acc[k].z, sh);
+                            acc[k].w += __shfl_xor_sync(tmask, acc[k].w, sh);
+                        }
+                    }
+                    if (gt == 0) write_row<V>(a, f, q, ok, acc, t, r == tk.row_start ? 0 : 1);
                 }
             }
-            if (gt == 0) write_row<V>(a, f, q, ok, acc, t, r == tk.row_start ? 0 : 1);
+        } else {
+            for (int r = tk.row_start + team; r < tk.row_end; r += teams) {
+                RowFrag f;
+                const int st = row_fragment(a, r, tk, f);
+                if (st == 1) {
+                    if (a.write_empty && gt == 0) write_zero_row<V>(a, f.orig, q, ok);
+                    continue;
+                }
+                if (st != 0) continue;
+                float4 acc[V];
+#pragma unroll
+                for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                gather_chunks<L, V, kPf, kUnit>(a, f.base + f.begin + gt * L, f.base + f.end,
+                                                team_lanes, gmask, lg, hq, ok, K4, acc);
+                for (int sh = L; sh < team_lanes; sh <<= 1) {
+#pragma unroll
+                    for (int i = 0; i < V; ++i) {
+                        acc[i].x += __shfl_xor_sync(tmask, acc[i].x, sh);
+                        acc[i].y += __shfl_xor_sync(tmask, acc[i].y, sh);
+                        acc[i].z += __shfl_xor_sync(tmask, acc[i].z, sh);
+                        acc[i].w += __shfl_xor_sync(tmask, acc[i].w, sh);
+                    }
+                }
+                if (gt == 0) write_row<V>(a, f, q, ok, acc, t, r == tk.row_start ? 0 : 1);
+            }
         }
     } else {
         // One row: the G groups take interleaved chunks, then reduce by
@@ -473,8 +495,9 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
         float4 acc[V];
 #pragma unroll
         for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        gather_chunks<L, V, !kStage && L >= 16 && L * V <= 32, kUnit>(a, f.base + f.begin + g * L, f.base + f.end, 32, gmask, lg, hq, ok,
-                            K4, acc);
+        gather_chunks<L, V, L >= 16 && L * V <= 32, kUnit>(a, f.base + f.begin + g * L,
+                                                           f.base + f.end, 32, gmask, lg, hq, ok,
+                                                           K4, acc);
 #pragma unroll
         for (int s = L; s < 32; s <<= 1) {
 #pragma unroll
@@ -1050,11 +1073,14 @@ void launch_vec(const SpmmArgs& a, bool stage, bool per_cta, cudaStream_t s) {
     dim3 grid(static_cast<unsigned>(ceil_div(a.n_slots, kWarpsPerCta)),
               static_cast<unsigned>(tiles));
     // Values NULL (every value 1.0): the instances without value loads and
-    // broadcasts (12% on configuration 5).  The short-row instance was 4%
-    // slower that way (configuration 4); launch_spmm_mean gives it an array
-    // of ones instead, so it never sees NULL.
+    // broadcasts (12% on configuration 5, 10% on configuration 4's short-row
+    // instance).
     if (stage) {
-        spmm_vec_kernel<L, V, true, false><<<grid, kThreads, 0, s>>>(a);
+        if (a.val == nullptr) {
+            spmm_vec_kernel<L, V, true, true><<<grid, kThreads, 0, s>>>(a);
+        } else {
+            spmm_vec_kernel<L, V, true, false><<<grid, kThreads, 0, s>>>(a);
+        }
     } else if (a.val == nullptr) {
         spmm_vec_kernel<L, V, false, true><<<grid, kThreads, 0, s>>>(a);
     } else {
@@ -1196,13 +1222,14 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
         // Short-row mode when tasks hold many rows on average (>= 16, e.g.
         // configuration 4's degree-4 rows, ~54 rows per task): each row's
         // offsets would otherwise be a dependent load on its critical path.
-        // It costs 8 KB of shared memory per CTA, taken from L1, so
-        // hub-heavy graphs with few rows per task keep the plain kernel.
+        // Graphs with fewer rows per task keep the plain kernel (its
+        // next-chunk prefetch and register budget serve their long rows:
+        // configurations 3 and 5 were 2% and 5% slower in short-row mode).
         // One CTA per task when one warp per task would leave the GPU's
         // last waves to a few long tasks (task_variant_flag); callers that
         // launch a list in pieces pass the whole list's choice.
         const bool per_cta = (task_variant_flag(ctx, a.n_tasks, flags) & CWLB_TASK_PER_CTA) != 0;
-        const bool stage = !per_cta && static_cast<int64_t>(n_rows) >= 16 * n_tasks;
+        const bool stage = !per_cta && static_cast<int64_t>(n_rows) >= kStageRowsPerTask * n_tasks;
         // Small tasks (a small S; not forced to one warp per task): runs of
         // tasks per warp, about kRunNnz nonzeros a run, at most 32 tasks.
         if (!per_cta && !stage && !sched && !det && !(flags & CWLB_TASK_PER_WARP)) {
@@ -1210,7 +1237,6 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
             if (per_task < kRunMaxTaskNnz)
                 a.run = static_cast<int32_t>(std::min<int64_t>(32, std::max<int64_t>(2, kRunNnz / per_task)));
         }
-        if (stage && a.val == nullptr && nnz > 0) a.val = ones_array(ctx, nnz);
         switch (L) {
             case 1: launch_vec_v<1>(V, a, stage, per_cta, s); break;
             case 2: launch_vec_v<2>(V, a, stage, per_cta, s); break;
@@ -1300,13 +1326,6 @@ spmm_mean_reference_kernel(const int32_t* __restrict__ rowoff, const int32_t* __
 }  // namespace
 
 namespace {
-__global__ void fill_ones_kernel(float* __restrict__ dst, size_t count) {
-    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
-    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
-         i += stride)
-        dst[i] = 1.0f;
-}
-
 // Sets *other when some value is not exactly 1.0f (compared as bits, so
 // -0.0 and NaN payloads count as other values).
 __global__ void values_other_kernel(const float* __restrict__ v, size_t count,
@@ -1320,19 +1339,6 @@ __global__ void values_other_kernel(const float* __restrict__ v, size_t count,
 }
 }  // namespace
 
-const float* ones_array(cwlb_ctx* ctx, int32_t count) {
-    const size_t n = static_cast<size_t>(count);
-    if (ctx->ones_count < n) {
-        float* d = ctx->ones.as<float>(n);
-        const unsigned blocks = static_cast<unsigned>(
-            std::min<int64_t>(ceil_div(static_cast<int64_t>(n), kThreads),
-                              static_cast<int64_t>(ctx->props.multiProcessorCount) * 8));
-        fill_ones_kernel<<<blocks, kThreads, 0, ctx->stream>>>(d, n);
-        CWLB_LAUNCH_CHECK("fill_ones_kernel");
-        ctx->ones_count = n;
-    }
-    return static_cast<const float*>(ctx->ones.ptr);
-}
 
 bool values_all_one(cwlb_ctx* ctx, const float* d_val, size_t count, unsigned int* d_flag) {
     if (count == 0) return true;
