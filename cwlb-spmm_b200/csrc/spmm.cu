@@ -194,9 +194,8 @@ struct VecCfg {
 //
 // kPrefetch: the next chunk's pair is loaded before this chunk's gathers, so
 // its latency overlaps them (6% on configuration 5, 1.5% on 2).  Used by the
-// <16,1>, <16,2> and <32,1> shapes outside short-row mode; short-row mode was
-// 10% slower with it (configuration 4), and wider or narrower shapes gain
-// registers and lose an occupancy step.
+// <16,1>, <16,2> and <32,1> shapes; wider or narrower shapes gain registers
+// and lose an occupancy step.
 template <int L, int V, bool kPrefetch, bool kUnit>
 __device__ __forceinline__ void gather_chunks(const SpmmArgs& a, int32_t start, int32_t end,
                                               int32_t step, unsigned gmask, int lg,
