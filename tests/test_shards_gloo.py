@@ -107,3 +107,65 @@ def test_gather_rows_rebuilds_the_sharded_input_on_every_rank(tmp_path, world):
     for r in range(world):
         got = np.load(out_path + f".{r}.npy")
         assert np.array_equal(got, X), f"rank {r}"
+
+
+def _rebalance_worker(rank, world, port, out_path):
+    """The bench's re-cut protocol (bench.py rebalance_shards) with gloo: every
+    rank 'times' its own shard (here a stand-in cost that prices short rows
+    far above the model), the times are all-gathered, every rank computes the
+    re-weighted cut, and the shards of that cut are aggregated and gathered."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import sys
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path[:0] = [os.path.join(root, "oracle"), os.path.join(root, "cwlb-spmm_b200")]
+        import cwlb_spmm as cs
+        from oracle import Oracle
+        oracle = Oracle()
+        rowoff, col, val, X = _graph()
+        costs = cs.SpmmCostParams(*COSTS)
+        deg = np.diff(rowoff.astype(np.int64))
+        true_cost = np.where(deg == 0, 6.0, deg + 17.0)
+        cut = cs.shard_bounds(rowoff, costs, world)
+        cuts = [cut.tolist()]
+        for _ in range(3):
+            t = torch.tensor([float(true_cost[cut[rank]:cut[rank + 1]].sum())], dtype=torch.float64)
+            times = [torch.zeros_like(t) for _ in range(world)]
+            dist.all_gather(times, t)
+            cut = cs.shard_bounds_rebalance(rowoff, costs, cut, [float(v) for v in times])
+            cuts.append(cut.tolist())
+        a, b = int(cut[rank]), int(cut[rank + 1])
+        ro, c, v = shards.shard_csr(rowoff, col, val, a, b)
+        origin, srow, scol, sval = oracle.sort_by_degree(ro, c, v)
+        tasks = oracle.partition(srow, COSTS, oracle.capacity_from_s(16, COSTS))
+        out = oracle.spmm_mean(srow, scol, sval, origin, X, tasks)
+        parts = [None] * world
+        dist.all_gather_object(parts, (cuts, out))
+        if rank == 0:
+            np.save(out_path, np.concatenate([p[1] for p in parts], axis=0))
+            np.save(out_path + ".cuts.npy", np.array([p[0] for p in parts]))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_rebalanced_cut_is_the_same_on_every_rank(tmp_path, oracle, world):
+    out_path = str(tmp_path / "rb.npy")
+    mp.spawn(_rebalance_worker, args=(world, _free_port(), out_path), nprocs=world, join=True)
+    cuts = np.load(out_path + ".cuts.npy")  # (ranks, rounds + 1, world + 1)
+    assert all(np.array_equal(cuts[0], cuts[r]) for r in range(world))
+    rowoff, col, val, X = _graph()
+    deg = np.diff(rowoff.astype(np.int64))
+    true_cost = np.where(deg == 0, 6.0, deg + 17.0)
+
+    def imbalance(c):
+        per = np.array([true_cost[c[g]:c[g + 1]].sum() for g in range(world)])
+        return per.max() / per.mean()
+
+    assert imbalance(cuts[0][-1]) < imbalance(cuts[0][0])
+    origin, srow, scol, sval = oracle.sort_by_degree(rowoff, col, val)
+    ref, cond = oracle.spmm_mean_f64(srow, scol, sval, origin, X)
+    from helpers import assert_mean_close
+    assert_mean_close(np.load(out_path), ref, cond, what="re-cut shards vs single")
