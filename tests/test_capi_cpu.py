@@ -43,6 +43,23 @@ def test_python_constants_equal_the_header_defines():
     assert checked >= 6
 
 
+def test_header_is_plain_c(tmp_path):
+    """include/cwlb_spmm.h is the C ABI: it compiles as pedantic C99 (and C++17)."""
+    import shutil
+    import subprocess
+    inc = os.path.dirname(cs.HEADER_PATH)
+    src = tmp_path / "h.c"
+    src.write_text('#include "cwlb_spmm.h"\nint main(void) { return CWLB_OK; }\n')
+    for cc, std in (("gcc", "-std=c99"), ("g++", "-std=c++17")):
+        if shutil.which(cc) is None:
+            pytest.skip(f"{cc} not installed")
+        lang = ["-x", "c++"] if cc == "g++" else []
+        r = subprocess.run([cc, std, "-Wall", "-Wextra", "-pedantic", "-Werror", f"-I{inc}",
+                            *lang, "-c", str(src), "-o", str(tmp_path / "h.o")],
+                           capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+
+
 def test_context_without_device_fails_loudly():
     try:
         import torch
