@@ -515,10 +515,11 @@ __global__ void __launch_bounds__(kThreads) spmm_vec_kernel(SpmmArgs a) {
 // Runs of small tasks (a small S): one warp per run of a.run consecutive
 // tasks.  Consecutive single-row tasks over adjacent nonzeros of the same row
 // (a hub row cut into many S-nonzero fragments) accumulate in the warp's
-// registers and reach the output with one write per run, an atomic add
-// unless the run covers the whole row: a.run times fewer atomics, and a.run
-// times less rounding from adding thousands of fragments to one output row
-// in float (at S = 16 a row of degree 10^6 receives 62,500 adds).  Every other
+// registers and reach the output with one atomic add per run onto the zeroed
+// row (a single task that covers its row whole is stored, as in
+// spmm_vec_kernel): a.run times fewer atomics, and a.run times less rounding
+// from adding thousands of fragments to one output row in float (at S = 16 a
+// row of degree 10^6 receives 62,500 adds).  Every other
 // task runs exactly as in spmm_vec_kernel (same lane groups, teams and
 // nonzero order), so every row that a single task covers whole is
 // bit-identical between the two kernels.
