@@ -106,3 +106,65 @@ def test_benchmark_config_scaled_parity(ctx, oracle, cfg, scale, staged):
                           what=f"config {cfg} / {scale} S={S} ({n_tasks} tasks)")
     if staged:
         assert staged_seen, "no candidate S reached the short-row staging instance"
+
+
+@pytest.mark.parametrize("cfg", [2, 3, 4, 5])
+def test_benchmark_config_full_size(ctx, cfg):
+    """The configurations at their full BASELINE size, where the CPU oracle is
+    too slow: size-independent properties of the degree sort (origin is a
+    permutation, degrees ascend, every sorted row is its original row) and of
+    the task list (tasks_check: every row covered, every nonzero owned once),
+    and the aggregation at the configuration's S, values passed as NULL as
+    bench.py passes them, against the float64 device reference over the
+    UNSORTED CSR (no sort, partition or task code in common) on every row."""
+    rowoff, col, val, X = graphs.build_config_torch(cfg, "cuda")
+    n, nnz, K = rowoff.numel() - 1, col.numel(), X.shape[1]
+    dev = X.device
+    assert bool((val == 1.0).all())
+    org = torch.empty(n, dtype=torch.int32, device=dev)
+    sro = torch.empty(n + 1, dtype=torch.int32, device=dev)
+    scol = torch.empty(nnz, dtype=torch.int32, device=dev)
+    sval = torch.empty(nnz, dtype=torch.float32, device=dev)
+    ctx.sort_by_degree_device(n, nnz, rowoff.data_ptr(), col.data_ptr(), val.data_ptr(),
+                              org.data_ptr(), sro.data_ptr(), scol.data_ptr(), sval.data_ptr())
+    torch.cuda.synchronize()
+    o = org.long()
+    assert torch.equal(torch.bincount(o, minlength=n), torch.ones(n, dtype=torch.long, device=dev))
+    deg_sorted = (sro[1:] - sro[:-1]).long()
+    deg_orig = (rowoff[1:] - rowoff[:-1]).long()
+    assert bool((deg_sorted[1:] >= deg_sorted[:-1]).all())
+    assert torch.equal(deg_sorted, deg_orig[o])
+    # Each sorted row holds its original row's column ids, in order.
+    starts = rowoff[:-1].long()[o]
+    idx = torch.repeat_interleave(starts - sro[:-1].long(), deg_sorted) + \
+        torch.arange(nnz, device=dev)
+    assert torch.equal(scol, col[idx])
+    del idx, starts
+
+    costs = cs.read_costs_one_per_line(COSTS_FILE)
+    S = graphs.CONFIGS[cfg]["S"]
+    ptr, n_tasks = ctx.partition_device(n, sro.data_ptr(), costs, cs.capacity_from_s(S, costs))
+    tasks = torch.as_tensor(_DevInt32(ptr, n_tasks * 4), device=dev).clone()
+    torch.cuda.synchronize()
+    chk = ctx.tasks_check(n, nnz, sro.data_ptr(), tasks.data_ptr(), n_tasks)
+    assert chk == dict(bad_tasks=0, uncovered_rows=0, nnz_coverage_errors=0)
+
+    out = torch.full((n, K), float("nan"), dtype=torch.float32, device=dev)
+    ctx.spmm_mean_device(n, nnz, sro.data_ptr(), scol.data_ptr(), 0, org.data_ptr(),
+                         X.data_ptr(), n, K, tasks.data_ptr(), n_tasks, out.data_ptr(),
+                         cs.ROWS_COVERED)
+    ref = torch.empty_like(out)
+    ctx.spmm_mean_reference_device(n, nnz, rowoff.data_ptr(), col.data_ptr(), val.data_ptr(),
+                                   X.data_ptr(), n, K, ref.data_ptr())
+    torch.cuda.synchronize()
+    assert ctx.take_device_errors() == 0
+    X.abs_()
+    scale = torch.empty_like(out)
+    ctx.spmm_mean_reference_device(n, nnz, rowoff.data_ptr(), col.data_ptr(), val.data_ptr(),
+                                   X.data_ptr(), n, K, scale.data_ptr())
+    torch.cuda.synchronize()
+    scale = torch.maximum(scale, ref.abs())
+    err = torch.where(scale > 0, (out - ref).abs() / scale, (out - ref).abs())
+    assert not bool(torch.isnan(out).any())
+    worst = float(err.max())
+    assert worst <= 1e-5, f"config {cfg}: max condition-relative error {worst:.3e}"
