@@ -213,7 +213,8 @@ void spmm_host_staged(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
             CWLB_CUDA(cudaEventRecord(ctx->pipe_t0[c], ks));
             cwlb::launch_spmm_mean(ctx, n_rows, nnz, d_ro, d_col, d_val, d_org, d_H, h_rows, K,
                                    d_tasks + t0, nt, d_out,
-                                   cwlb::kFlagOutCleared | cwlb::task_variant_flag(ctx, n_tasks, 0));
+                                   cwlb::kFlagOutCleared | cwlb::task_variant_flag(ctx, n_tasks, 0),
+                                   nullptr, 0, cwlb::task_run_length(nnz, n_tasks));
             CWLB_CUDA(cudaEventRecord(ctx->pipe_t1[c], ks));
             launched[c] = true;
         }

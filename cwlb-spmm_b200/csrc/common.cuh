@@ -105,11 +105,14 @@ constexpr uint32_t kFlagSplitZeroed = 1u << 30;
 // choice to every piece, so that every row a task covers whole comes out as
 // one launch would give it.
 uint32_t task_variant_flag(const cwlb_ctx* ctx, int64_t n_tasks, uint32_t flags);
+// Tasks per warp run (spmm_run_kernel) for a list of n_tasks over nnz
+// nonzeros: 1 (no runs) unless tasks average fewer than 128 nonzeros.
+int32_t task_run_length(int64_t nnz, int64_t n_tasks);
 void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t* rowoff,
                       const int32_t* col, const float* val, const int32_t* origin,
                       const float* H, int64_t h_rows, int64_t K, const cwlb_task* tasks,
                       int64_t n_tasks, float* out, uint32_t flags,
-                      const int32_t* sched = nullptr, int64_t n_slots = 0);
+                      const int32_t* sched = nullptr, int64_t n_slots = 0, int32_t run = -1);
 // Copies of caller memory for the host-buffer entry points (staging.cu).
 // copy_to_device is asynchronous on `s`; once it returns, the source may be
 // reused; copy_to_host returns when `dst` holds the data.  Large pageable

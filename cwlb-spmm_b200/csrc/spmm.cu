@@ -1130,6 +1130,13 @@ void pick_vec_shape(int64_t K4, int& L, int& V) {
 
 }  // namespace
 
+int32_t task_run_length(int64_t nnz, int64_t n_tasks) {
+    if (n_tasks <= 0) return 1;
+    const int64_t per_task = std::max<int64_t>(1, nnz / n_tasks);
+    if (per_task >= kRunMaxTaskNnz) return 1;
+    return static_cast<int32_t>(std::min<int64_t>(32, std::max<int64_t>(2, kRunNnz / per_task)));
+}
+
 uint32_t task_variant_flag(const cwlb_ctx* ctx, int64_t n_tasks, uint32_t flags) {
     if (flags & (CWLB_TASK_PER_WARP | CWLB_TASK_PER_CTA | kFlagWarpTasks))
         return flags & (CWLB_TASK_PER_WARP | CWLB_TASK_PER_CTA | kFlagWarpTasks);
@@ -1142,7 +1149,7 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
                       const int32_t* col, const float* val, const int32_t* origin,
                       const float* H, int64_t h_rows, int64_t K, const cwlb_task* tasks,
                       int64_t n_tasks, float* out, uint32_t flags, const int32_t* sched,
-                      int64_t n_slots) {
+                      int64_t n_slots, int32_t run) {
     if (K <= 0 || n_rows <= 0) return;
     cudaStream_t s = ctx->stream;
     const bool covered = (flags & CWLB_ROWS_COVERED) != 0;
@@ -1231,11 +1238,12 @@ void launch_spmm_mean(cwlb_ctx* ctx, int32_t n_rows, int32_t nnz, const int32_t*
         const bool per_cta = (task_variant_flag(ctx, a.n_tasks, flags) & CWLB_TASK_PER_CTA) != 0;
         const bool stage = !per_cta && static_cast<int64_t>(n_rows) >= kStageRowsPerTask * n_tasks;
         // Small tasks (a small S; not forced to one warp per task): runs of
-        // tasks per warp, about kRunNnz nonzeros a run, at most 32 tasks.
+        // tasks per warp, about kRunNnz nonzeros a run, at most 32 tasks
+        // (task_run_length; a caller launching one list in pieces passes the
+        // whole list's run length).
         if (!per_cta && !stage && !sched && !det && !(flags & CWLB_TASK_PER_WARP)) {
-            const int64_t per_task = std::max<int64_t>(1, nnz / n_tasks);
-            if (per_task < kRunMaxTaskNnz)
-                a.run = static_cast<int32_t>(std::min<int64_t>(32, std::max<int64_t>(2, kRunNnz / per_task)));
+            const int32_t r = run >= 0 ? run : task_run_length(nnz, n_tasks);
+            if (r > 1) a.run = r;
         }
         switch (L) {
             case 1: launch_vec_v<1>(V, a, stage, per_cta, s); break;

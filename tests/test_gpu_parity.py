@@ -395,12 +395,15 @@ def test_unit_values_are_not_copied_but_give_the_same_result(ctx, oracle):
         assert np.abs(out - o32).max() <= 1e-4
 
 
-@pytest.mark.parametrize("unit,K", [(True, 16), (False, 16), (True, 1100)])
-def test_chunked_host_call_matches_single_shot(ctx, oracle, unit, K):
+@pytest.mark.parametrize("unit,K,S", [(True, 16, 256), (False, 16, 256), (True, 1100, 256),
+                                      (True, 16, 16), (False, 64, 8)])
+def test_chunked_host_call_matches_single_shot(ctx, oracle, unit, K, S):
     """Host-buffer calls of 4M+ nonzeros with tasks in partition order copy
     their nonzeros in chunks and aggregate each chunk as soon as it arrives.
     The same tasks in reverse order cannot be chunked (one copy, one launch):
-    both give the oracle's result, and whole rows agree bit for bit."""
+    both give the oracle's result, and whole rows agree bit for bit.  At
+    S = 16 and 8 every chunk runs warp runs of small tasks with the whole
+    list's run length."""
     rng = np.random.default_rng(91 if unit else 92)
     n = 50000
     rowoff, col, val = random_csr(rng, n, 200, hubs=3, hub_factor=50)
@@ -409,7 +412,7 @@ def test_chunked_host_call_matches_single_shot(ctx, oracle, unit, K):
     assert len(col) >= (1 << 22)
     H = rng.standard_normal((n, K)).astype(np.float32)
     costs = [0.1, 0.6, 0.4, 0.9]
-    origin, srow, scol, sval, cap, tasks = _oracle_pipeline(oracle, rowoff, col, val, costs, 256)
+    origin, srow, scol, sval, cap, tasks = _oracle_pipeline(oracle, rowoff, col, val, costs, S)
     tk = np.asarray(tasks).reshape(-1, 4)
     order = cs.CSR_Order(srow, scol, sval, origin)
     call = ctx.spmmKernel if K <= 1024 else ctx.spmmKernelLargeKFallback
