@@ -473,3 +473,51 @@ def test_task_runs_match_one_warp_per_task(ctx, oracle, K, S):
     whole = np.array(whole, np.int64)
     assert len(whole) > n // 4
     assert np.array_equal(runs[whole].view(np.uint32), warp[whole].view(np.uint32))
+
+
+def test_task_runs_keep_a_huge_hub_row_within_tolerance(ctx, oracle):
+    """A row of degree 2^20 at S = 16 is cut into 65,536 fragment tasks.  Warp
+    runs add each run's fragments in registers and reach the row with ~2,000
+    float atomics instead of 65,536, which keeps the row within the
+    condition-relative 1e-5 (one warp per task, forced, is reported beside it:
+    its accumulated rounding is what the runs remove)."""
+    rng = np.random.default_rng(41)
+    hub = 1 << 20
+    d = np.concatenate([rng.integers(0, 6, 20_000), [hub]])
+    rowoff = np.zeros(len(d) + 1, np.int64)
+    rowoff[1:] = np.cumsum(d)
+    n_cols = hub
+    col = rng.integers(0, n_cols, int(rowoff[-1])).astype(np.int32)
+    col[rowoff[-2]:] = np.arange(hub, dtype=np.int32)  # the hub row: every column once
+    rowoff = rowoff.astype(np.int32)
+    val = np.ones(len(col), np.float32)
+    K = 16
+    # Positive features: the fragments' partial sums all share a sign, so the
+    # float adds onto the hub's output row round in the same direction.
+    X = graphs.uniform_features_np(n_cols, K, seed=42, lo=0.0, hi=1.0)
+    costs = cs.SpmmCostParams(0.02, 0.7, 0.3, 0.5)
+    p = _device_pipeline(ctx, rowoff, col, val, X, costs, 16)
+    torch.cuda.synchronize()
+    n, nnz = p["n"], p["nnz"]
+
+    def run(flags):
+        out = torch.full((n, K), float("nan"), dtype=torch.float32, device="cuda:0")
+        ctx.spmm_mean_device(n, nnz, p["sro"].data_ptr(), p["scol"].data_ptr(), 0,
+                             p["org"].data_ptr(), p["X"].data_ptr(), n_cols, K, p["t_ptr"],
+                             p["n_tasks"], out.data_ptr(), cs.ROWS_COVERED | flags)
+        torch.cuda.synchronize()
+        assert ctx.take_device_errors() == 0
+        return out.cpu().numpy()
+
+    o = [t.cpu().numpy() for t in (p["sro"], p["scol"][:nnz], p["org"])]
+    ref, cond = oracle.spmm_mean_f64(o[0], o[1], val, o[2], X)
+    from helpers import rel_errors
+    runs, warp = run(0), run(cs.TASK_PER_WARP)
+    hub_row = len(d) - 1
+    e_runs = float(rel_errors(runs[hub_row:hub_row + 1], ref[hub_row:hub_row + 1],
+                              cond[hub_row:hub_row + 1]).max())
+    e_warp = float(rel_errors(warp[hub_row:hub_row + 1], ref[hub_row:hub_row + 1],
+                              cond[hub_row:hub_row + 1]).max())
+    print(f"hub row of degree {hub}: warp runs {e_runs:.2e}, one warp per task {e_warp:.2e}")
+    assert_mean_close(runs, ref, cond, what="warp runs, huge hub row")
+    assert e_runs < e_warp
